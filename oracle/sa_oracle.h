@@ -1,0 +1,143 @@
+/*
+ * sa_oracle.h -- CPU restatement of the reference's decode-time sparse-KV path.
+ *
+ * TEST INFRASTRUCTURE ONLY. This is the parity checker, never the product:
+ * only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg may
+ * load it. The product library (libsa_b200.so) neither links nor calls it.
+ *
+ * Every function restates one piece of the reference (ZjuXxxc/solidattention-repro,
+ * paths relative to that project) in plain C, keeping the reference's
+ * floating-point operation order so that results are bit-identical to the
+ * reference compiled with g++ -O2 on x86-64 (no FMA contraction):
+ *
+ *   sao_half_to_float          cpp/src/attention_reference.cpp:30-53
+ *   sao_ref_float_to_half      cpp/src/attention_reference.cpp:11-28 (non-RNE;
+ *                              only to regenerate the reference's own fixtures)
+ *   sao_attention              cpp/src/attention_reference.cpp:55-96
+ *   sao_select_shared_blocks   cpp/src/selection.cpp:96-147
+ *   sao_build_representatives  cpp/src/selection.cpp:12-94
+ *   sao_c1_fixture             cpp/src/attention_main.cpp:131-156
+ *   sao_c21_fixture            cpp/src/selection_main.cpp:113-154
+ *   sao_gather_packed          cpp/src/selection_main.cpp:196-218 and
+ *                              cpp/src/qwen_chain_main.cpp:360-395 (token order)
+ *   sao_lifecycle_run          cpp/src/kv_lifecycle_main.cpp:25-113
+ *
+ * Parity of this restatement is pinned against the reference compiled from
+ * its own sources (oracle/_ref) and against the reference's published known
+ * answers (tests/golden/).
+ */
+#ifndef SA_ORACLE_H
+#define SA_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+float sao_half_to_float(uint16_t value);
+uint16_t sao_float_to_half_rne(float value);
+uint16_t sao_ref_float_to_half(float value);
+void sao_half_to_float_n(const uint16_t* in, float* out, size_t n);
+void sao_float_to_half_rne_n(const float* in, uint16_t* out, size_t n);
+
+/* GQA attention over a packed token-major buffer [tokens][2][kv_heads][head_dim]
+ * (K plane, then V plane per token). out: [query_heads][head_dim] FP32.
+ * Returns 0, or -1 on the reference's invalid-dimension condition. */
+int sao_attention(const uint16_t* interleaved_kv, const float* query,
+                  size_t tokens, size_t query_heads, size_t kv_heads,
+                  size_t head_dim, float scale, float* out);
+
+/* Representative scoring + init/local forcing + stable top-k.
+ * query [query_heads][head_dim], representatives [query_heads][blocks][head_dim].
+ * block_ids_out receives the chosen ids ascending (capacity budget_blocks),
+ * *n_ids_out their count; scores_out (nullable) receives mean_head_scores[blocks].
+ * Returns 0 or -1 on invalid dimensions. */
+int sao_select_shared_blocks(const float* query, const float* representatives,
+                             size_t query_heads, size_t blocks,
+                             size_t head_dim, size_t budget_blocks,
+                             size_t init_blocks, size_t local_blocks,
+                             int64_t* block_ids_out, size_t* n_ids_out,
+                             float* scores_out);
+
+/* Per-KV-head selection: the unmodified shared selection applied to each
+ * group of `group` consecutive query heads (group == query_heads is the
+ * reference's shared mode). ids_out: [query_heads/group][budget_blocks].
+ * scores_out (nullable): [query_heads/group][blocks]. */
+int sao_select_grouped(const float* query, const float* representatives,
+                       size_t query_heads, size_t group, size_t blocks,
+                       size_t head_dim, size_t budget_blocks,
+                       size_t init_blocks, size_t local_blocks,
+                       int64_t* ids_out, float* scores_out);
+
+/* Local-causal received-mass representatives.
+ * prompt_queries [query_heads][tokens][head_dim] FP32; interleaved_kv as above.
+ * values_out [query_heads][tokens/block_tokens][head_dim];
+ * offsets_out [query_heads][tokens/block_tokens][topk] (in-block offsets,
+ * rank order); received_out (nullable) [query_heads][tokens]. */
+int sao_build_representatives(const float* prompt_queries,
+                              const uint16_t* interleaved_kv, size_t tokens,
+                              size_t query_heads, size_t kv_heads,
+                              size_t head_dim, size_t block_tokens,
+                              size_t local_window, size_t topk,
+                              float* values_out, int64_t* offsets_out,
+                              float* received_out);
+
+/* The reference's deterministic fixtures. */
+void sao_c1_fixture(uint16_t* kv /* 128*2*8*128 */, float* query /* 16*128 */);
+void sao_c21_fixture(uint16_t* kv /* 512*2*8*128 */,
+                     float* prompt_queries /* 16*512*128 */,
+                     float* query /* 16*128: last prompt position */);
+
+/* Packed gather: selected blocks (block ids into `store`, ascending as the
+ * selector returns them) followed by `tail_tokens` rows of `tail`, copied into
+ * `out` as one token-major buffer. token_values = 2*kv_heads*head_dim. */
+void sao_gather_packed(const uint16_t* store, const int64_t* block_ids,
+                       size_t n_blocks, size_t block_tokens,
+                       const uint16_t* tail, size_t tail_tokens,
+                       size_t token_values, uint16_t* out);
+
+/* KV lifecycle: append decode tokens to each layer's tail and seal the oldest
+ * block while tail >= local_tokens + block_tokens. Token bytes follow the
+ * reference's synthetic formula (layer*1009 + token*37 + value*13) & 0xffff.
+ * store (nullable) has room for layers*capacity_blocks blocks; every sealed
+ * block is written at (layer*capacity_blocks + initial_blocks + sealed)*block.
+ * rep_indices_out (nullable) receives [total_seals][q_heads][4].
+ * Results: per-layer sealed counts/generation, final tail tokens, audits. */
+typedef struct {
+  size_t sealed_total;
+  size_t representative_audits;
+  size_t tail_tokens_layer0;
+  size_t generation_layer0;
+  size_t capacity_blocks;
+} sao_lifecycle_result;
+
+int sao_lifecycle_run(size_t layers, size_t q_heads, size_t kv_heads,
+                      size_t head_dim, size_t block_tokens,
+                      size_t local_tokens, size_t decode_tokens,
+                      size_t initial_blocks, uint16_t* store,
+                      int64_t* rep_indices_out, sao_lifecycle_result* result);
+
+/* One CPU decode step over `layers` layers (see sa_oracle.c). pool
+ * [pool_blocks][block_tokens][2][kv_heads][head_dim] FP16; table
+ * [layers][table_stride]; reps [layers][query_heads][blocks][head_dim];
+ * query [layers][query_heads][head_dim]; tail_block [layers];
+ * ids_out [layers][kv_heads][budget]; out [layers][query_heads][head_dim]. */
+int sao_sparse_step(const uint16_t* pool, const int32_t* table,
+                    size_t table_stride, const float* reps, const float* query,
+                    const int32_t* tail_block, size_t tail_len, size_t layers,
+                    size_t query_heads, size_t kv_heads, size_t head_dim,
+                    size_t block_tokens, size_t blocks, size_t budget,
+                    size_t init, size_t local, float scale, int threads,
+                    int64_t* ids_out, float* out);
+
+/* FNV-1a over 64-bit words, as the C2.1 driver hashes representative offsets
+ * (cpp/src/selection_main.cpp:167-171). */
+uint64_t sao_fnv_offsets(const int64_t* values, size_t n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif
