@@ -1,0 +1,889 @@
+// sa_api.cu -- implementation of the C ABI declared in include/sa_b200.h.
+//
+// Host-side runtime of the sparse-KV path: argument validation with the
+// reference's error conditions, TMA descriptor creation, workspace plans,
+// the AcceleratorBackend-style handle (host buffers, event timings) and the
+// paged decode context (pool, free list, block tables, tails, seal).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "sa_internal.h"
+
+namespace sa {
+
+namespace {
+thread_local std::string g_last_error;
+}
+
+sa_status fail(sa_status status, const std::string& message) {
+  g_last_error = message;
+  return status;
+}
+
+sa_status cuda_status(cudaError_t err, const char* what) {
+  if (err == cudaSuccess) return SA_OK;
+  return fail(SA_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
+}
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Runs the caller's device choice on entry and restores it on exit.
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int device) {
+    if (cudaGetDevice(&previous_) != cudaSuccess) previous_ = -1;
+    if (device >= 0 && device != previous_) ok_ = cudaSetDevice(device) == cudaSuccess;
+  }
+  ~DeviceGuard() {
+    if (previous_ >= 0) cudaSetDevice(previous_);
+  }
+  bool ok() const { return ok_; }
+
+ private:
+  int previous_ = -1;
+  bool ok_ = true;
+};
+
+}  // namespace
+
+sa_status ensure_smem_limit(const void* kernel, int bytes, int* configured_per_device) {
+  int dev = 0;
+  SA_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(SA_ERR_UNSUPPORTED, "device index above 63");
+  if (configured_per_device[dev] >= bytes) return SA_OK;
+  SA_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  configured_per_device[dev] = bytes;
+  return SA_OK;
+}
+
+sa_status make_row_tensor_map(CUtensorMap* map, const void* base, uint64_t row_elems,
+                              uint64_t rows) {
+  auto encode = tensor_map_encoder();
+  if (!encode) return fail(SA_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+    return fail(SA_ERR_INVALID_ARG, "KV buffer must be 16-byte aligned");
+  if (rows == 0 || rows > 0xffffffffull) return fail(SA_ERR_UNSUPPORTED, "KV rows out of TMA range");
+  const cuuint64_t dims[2] = {row_elems, rows};
+  const cuuint64_t strides[1] = {row_elems * sizeof(uint16_t)};
+  const cuuint32_t box[2] = {64, (cuuint32_t)kBlockTokens};
+  const cuuint32_t elem_strides[2] = {1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims,
+                            strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(SA_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return SA_OK;
+}
+
+}  // namespace sa
+
+using namespace sa;
+
+// =============================================================== status
+
+struct sa_backend {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev[5] = {};
+  void* d_kv = nullptr;
+  size_t kv_cap = 0;
+  float* d_q = nullptr;
+  size_t q_cap = 0;
+  float* d_out = nullptr;
+  size_t out_cap = 0;
+  float* d_checksum = nullptr;
+  void* d_ws = nullptr;
+  size_t ws_cap = 0;
+  uint8_t* d_io = nullptr;
+  size_t io_cap = 0;
+};
+
+struct sa_ctx {
+  sa_ctx_config cfg{};
+  int num_sl = 0, group = 0, n_sel_groups = 0, table_pad = 0;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  CtxDev dev{};
+  CUtensorMap pool_map{};
+  int32_t* selected = nullptr;
+  int32_t* selected_count = nullptr;
+  float* scores = nullptr;
+  int* select_counters = nullptr;
+  float* attn_partial = nullptr;
+  int* attn_counters = nullptr;
+  int attn_splits = 1, attn_split_entries = 1;
+  // staging for sa_ctx_step_host
+  float* d_query = nullptr;
+  void* d_kv_new = nullptr;
+  void* d_out = nullptr;
+  uint32_t* h_status = nullptr;  // pinned
+  std::vector<uint8_t> prefilled;
+  uint64_t launches = 0;
+};
+
+extern "C" {
+
+SA_API const char* sa_status_string(sa_status status) {
+  switch (status) {
+    case SA_OK: return "ok";
+    case SA_ERR_INVALID_ARG: return "invalid argument";
+    case SA_ERR_UNSUPPORTED: return "unsupported";
+    case SA_ERR_CAPACITY: return "capacity exceeded";
+    case SA_ERR_CUDA: return "CUDA error";
+    case SA_ERR_DEVICE: return "device status error";
+    case SA_ERR_TIMEOUT: return "device wait timed out";
+    case SA_ERR_NO_MEMORY: return "out of memory";
+    default: return "unknown status";
+  }
+}
+
+SA_API const char* sa_last_error(void) { return g_last_error.c_str(); }
+
+SA_API const char* sa_version(void) { return "sa_b200 0.1 sm_100a"; }
+
+// ===================================================== stateless kernels
+
+SA_API size_t sa_attention_workspace_size(size_t tokens, size_t query_heads, size_t kv_heads) {
+  if (kv_heads == 0 || query_heads % kv_heads != 0) return 0;
+  const int entries = (int)((tokens + kBlockTokens - 1) / kBlockTokens);
+  int split = 1;
+  const int units = (int)kv_heads;
+  const int nsplit = attention_plan_splits(units, std::max(entries, 1), &split);
+  return attention_scratch_bytes(units, nsplit, (int)(query_heads / kv_heads)) +
+         (size_t)units * sizeof(int) + 256;
+}
+
+SA_API sa_status sa_attention_packed(const uint16_t* kv, const float* query, size_t tokens,
+                                     size_t query_heads, size_t kv_heads, size_t head_dim,
+                                     float scale, void* out, int out_fp16, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  if (!kv || !query || !out) return fail(SA_ERR_INVALID_ARG, "attention: null pointer");
+  if (kv_heads == 0 || query_heads % kv_heads != 0 || tokens == 0)
+    return fail(SA_ERR_INVALID_ARG, "invalid GQA attention dimensions");
+  if (head_dim != (size_t)kHeadDim) return fail(SA_ERR_UNSUPPORTED, "attention: head_dim must be 128");
+  const size_t need = sa_attention_workspace_size(tokens, query_heads, kv_heads);
+  if (!workspace || workspace_bytes < need)
+    return fail(SA_ERR_CAPACITY, "attention: workspace smaller than sa_attention_workspace_size()");
+  if (tokens > 0xffffffffull) return fail(SA_ERR_UNSUPPORTED, "attention: too many tokens");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CUtensorMap map;
+  sa_status st = make_row_tensor_map(&map, kv, 2 * kv_heads * kHeadDim, tokens);
+  if (st != SA_OK) return st;
+  const int entries = (int)((tokens + kBlockTokens - 1) / kBlockTokens);
+  const int units = (int)kv_heads;
+  AttnParams p{};
+  p.kv_heads = (int)kv_heads;
+  p.group = (int)(query_heads / kv_heads);
+  p.num_sl = 1;
+  p.pool_blocks = entries;
+  p.sel_ids = nullptr;
+  p.sel_count = nullptr;
+  p.sel_stride = entries;
+  p.n_sel_groups = 1;
+  p.kv_per_sel_group = (int)kv_heads;
+  p.fixed_nsel = (int)(tokens / kBlockTokens);
+  p.table = nullptr;
+  p.table_stride = entries;
+  p.tail_block = nullptr;
+  p.tail_len = nullptr;
+  p.fixed_tail_block = (int)(tokens / kBlockTokens);
+  p.fixed_tail_len = (int)(tokens % kBlockTokens);
+  p.query = query;
+  p.out = out;
+  p.out_fp16 = out_fp16;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.max_splits = attention_plan_splits(units, entries, &p.split_entries);
+  char* ws = static_cast<char*>(workspace);
+  const size_t partial_bytes = attention_scratch_bytes(units, p.max_splits, p.group);
+  p.partial = reinterpret_cast<float*>(ws);
+  p.counters = reinterpret_cast<int*>(ws + ((partial_bytes + 255) & ~size_t(255)));
+  p.status = nullptr;
+  if (p.max_splits > 1)
+    SA_CUDA_TRY(cudaMemsetAsync(p.counters, 0, (size_t)units * sizeof(int), s));
+  return launch_attention(p, map, s);
+}
+
+SA_API size_t sa_select_workspace_size(size_t query_heads, size_t group, size_t blocks) {
+  if (group == 0 || query_heads % group != 0) return 0;
+  const size_t n_groups = query_heads / group;
+  const size_t cap = (blocks + 3) & ~size_t(3);
+  return n_groups * cap * sizeof(float) + n_groups * sizeof(int) + 256;
+}
+
+SA_API sa_status sa_select_blocks(const float* query, const float* reps, int64_t stride_head,
+                                  int64_t stride_block, int64_t stride_dim, size_t query_heads,
+                                  size_t group, size_t blocks, size_t head_dim,
+                                  size_t budget_blocks, size_t init_blocks, size_t local_blocks,
+                                  int32_t* block_ids_out, float* scores_out, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  // The reference's own validation (cpp/src/selection.cpp:99-105).
+  if (!query || !reps || query_heads == 0 || blocks == 0 || head_dim == 0 || budget_blocks == 0 ||
+      budget_blocks > blocks || init_blocks + local_blocks > budget_blocks)
+    return fail(SA_ERR_INVALID_ARG, "invalid representative selection dimensions");
+  if (group == 0 || query_heads % group != 0)
+    return fail(SA_ERR_INVALID_ARG, "select: group must divide query_heads");
+  if (!block_ids_out) return fail(SA_ERR_INVALID_ARG, "select: null block_ids_out");
+  if (blocks > (size_t)select_max_blocks())
+    return fail(SA_ERR_UNSUPPORTED, "select: more than 16384 blocks");
+  const size_t need = sa_select_workspace_size(query_heads, group, blocks);
+  if (!workspace || workspace_bytes < need)
+    return fail(SA_ERR_CAPACITY, "select: workspace smaller than sa_select_workspace_size()");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t n_groups = query_heads / group;
+  const int cap = (int)((blocks + 3) & ~size_t(3));
+  SelectParams p{};
+  p.query = query;
+  p.reps = reps;
+  p.s_sl = 0;
+  p.s_head = stride_head;
+  p.s_block = stride_block;
+  p.s_dim = stride_dim;
+  p.qh = (int)query_heads;
+  p.group = (int)group;
+  p.n_groups = (int)n_groups;
+  p.d = (int)head_dim;
+  p.num_sl = 1;
+  p.nb = nullptr;
+  p.fixed_nb = (int)blocks;
+  p.budget = (int)budget_blocks;
+  p.init = (int)init_blocks;
+  p.local = (int)local_blocks;
+  p.ids = block_ids_out;
+  p.counts = nullptr;
+  char* ws = static_cast<char*>(workspace);
+  p.scores = reinterpret_cast<float*>(ws);
+  p.counters = reinterpret_cast<int*>(ws + n_groups * cap * sizeof(float));
+  p.status = nullptr;
+  // A caller's reps extent along blocks is `blocks`: keep vector loads inside it.
+  p.nb_cap = (stride_block == 1 && blocks % 4 != 0) ? (int)blocks : cap;
+  SA_CUDA_TRY(cudaMemsetAsync(p.counters, 0, n_groups * sizeof(int), s));
+  const int row = p.nb_cap;
+  sa_status st = launch_select(p, s);
+  if (st != SA_OK) return st;
+  if (scores_out)
+    SA_CUDA_TRY(cudaMemcpy2DAsync(scores_out, blocks * sizeof(float), p.scores,
+                                  (size_t)row * sizeof(float), blocks * sizeof(float), n_groups,
+                                  cudaMemcpyDeviceToDevice, s));
+  return SA_OK;
+}
+
+SA_API sa_status sa_build_representatives(const float* prompt_queries, const uint16_t* kv,
+                                          size_t tokens, size_t query_heads, size_t kv_heads,
+                                          size_t head_dim, size_t block_tokens,
+                                          size_t local_window, size_t topk, float* values_out,
+                                          int32_t* offsets_out, void* stream) {
+  // The reference's own validation (cpp/src/selection.cpp:17-22).
+  if (!prompt_queries || !kv || tokens == 0 || kv_heads == 0 || query_heads % kv_heads != 0 ||
+      block_tokens == 0 || tokens % block_tokens != 0 || local_window == 0 || topk == 0 ||
+      topk > block_tokens)
+    return fail(SA_ERR_INVALID_ARG, "invalid local-causal representative dimensions");
+  if (block_tokens != (size_t)kBlockTokens)
+    return fail(SA_ERR_UNSUPPORTED, "representatives: block_tokens must be 32");
+  if (!values_out) return fail(SA_ERR_INVALID_ARG, "representatives: null values_out");
+  RepParams p{};
+  p.kv = kv;
+  p.row_stride = (int64_t)(2 * kv_heads * head_dim);
+  p.table = nullptr;
+  p.table_offset = 0;
+  p.kv_heads = (int)kv_heads;
+  p.q = prompt_queries;
+  p.qh = (int)query_heads;
+  p.d = (int)head_dim;
+  p.tokens = (int)tokens;
+  p.blocks = (int)(tokens / block_tokens);
+  p.window = (int)local_window;
+  p.topk = (int)topk;
+  p.scale = 1.0f / std::sqrt((float)head_dim);
+  p.values = values_out;
+  p.o_head = (int64_t)p.blocks * head_dim;
+  p.o_block = (int64_t)head_dim;
+  p.o_dim = 1;
+  p.offsets = offsets_out;
+  p.status = nullptr;
+  return launch_build_reps(p, static_cast<cudaStream_t>(stream));
+}
+
+SA_API sa_status sa_pack_kv_fp16(uint16_t* packed, const float* key, const float* value,
+                                 size_t token, size_t elements, void* stream) {
+  if (!packed || !key || !value) return fail(SA_ERR_INVALID_ARG, "pack: null pointer");
+  return launch_pack_kv(packed, key, value, token, elements, static_cast<cudaStream_t>(stream));
+}
+
+// ========================================================= backend handle
+
+SA_API sa_status sa_backend_create(int device, sa_backend** out) {
+  if (!out) return fail(SA_ERR_INVALID_ARG, "backend: null out");
+  *out = nullptr;
+  DeviceGuard guard(device);
+  if (!guard.ok()) return fail(SA_ERR_CUDA, "backend: cudaSetDevice failed");
+  auto* b = new (std::nothrow) sa_backend();
+  if (!b) return fail(SA_ERR_NO_MEMORY, "backend: allocation failed");
+  b->device = device;
+  sa_status st = cuda_status(cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking),
+                             "cudaStreamCreateWithFlags");
+  for (int i = 0; st == SA_OK && i < 5; ++i) st = cuda_status(cudaEventCreate(&b->ev[i]), "cudaEventCreate");
+  if (st == SA_OK) st = cuda_status(cudaMalloc(&b->d_checksum, sizeof(float)), "cudaMalloc checksum");
+  if (st != SA_OK) {
+    sa_backend_destroy(b);
+    return st;
+  }
+  *out = b;
+  return SA_OK;
+}
+
+SA_API sa_status sa_backend_destroy(sa_backend* b) {
+  if (!b) return SA_OK;
+  DeviceGuard guard(b->device);
+  if (b->stream) cudaStreamSynchronize(b->stream);
+  cudaFree(b->d_kv);
+  cudaFree(b->d_q);
+  cudaFree(b->d_out);
+  cudaFree(b->d_checksum);
+  cudaFree(b->d_ws);
+  cudaFree(b->d_io);
+  for (auto& e : b->ev)
+    if (e) cudaEventDestroy(e);
+  if (b->stream) cudaStreamDestroy(b->stream);
+  delete b;
+  return SA_OK;
+}
+
+SA_API const char* sa_backend_name(const sa_backend*) { return "b200-sm100a"; }
+
+SA_API sa_status sa_backend_host_alloc(sa_backend* b, size_t bytes, void** out) {
+  if (!b || !out) return fail(SA_ERR_INVALID_ARG, "host_alloc: null argument");
+  DeviceGuard guard(b->device);
+  return cuda_status(cudaHostAlloc(out, bytes, cudaHostAllocDefault), "cudaHostAlloc");
+}
+
+SA_API sa_status sa_backend_host_free(sa_backend* b, void* pointer) {
+  if (!b) return fail(SA_ERR_INVALID_ARG, "host_free: null backend");
+  return cuda_status(cudaFreeHost(pointer), "cudaFreeHost");
+}
+
+}  // extern "C"
+
+namespace {
+sa_status grow(void** ptr, size_t* cap, size_t bytes) {
+  if (bytes <= *cap) return SA_OK;
+  cudaFree(*ptr);
+  *ptr = nullptr;
+  *cap = 0;
+  SA_CUDA_TRY(cudaMalloc(ptr, bytes));
+  *cap = bytes;
+  return SA_OK;
+}
+}  // namespace
+
+extern "C" {
+
+SA_API sa_status sa_backend_attention(sa_backend* b, const uint16_t* kv_host,
+                                      const float* query_host, size_t tokens, size_t query_heads,
+                                      size_t kv_heads, size_t head_dim, float scale, int flags,
+                                      float* out_host, sa_timings* timings) {
+  if (!b || !kv_host || !query_host) return fail(SA_ERR_INVALID_ARG, "backend attention: null pointer");
+  if (kv_heads == 0 || query_heads % kv_heads != 0 || tokens == 0)
+    return fail(SA_ERR_INVALID_ARG, "invalid GQA attention dimensions");
+  if (head_dim != (size_t)kHeadDim) return fail(SA_ERR_UNSUPPORTED, "attention: head_dim must be 128");
+  if ((flags & (SA_ATTN_COPY_OUTPUT | SA_ATTN_CONSUME)) && !out_host)
+    return fail(SA_ERR_INVALID_ARG, "backend attention: null out_host");
+  DeviceGuard guard(b->device);
+  const size_t kv_bytes = tokens * 2 * kv_heads * head_dim * sizeof(uint16_t);
+  const size_t q_bytes = query_heads * head_dim * sizeof(float);
+  const size_t ws_bytes = sa_attention_workspace_size(tokens, query_heads, kv_heads);
+  sa_status st;
+  if ((st = grow(&b->d_kv, &b->kv_cap, kv_bytes)) != SA_OK) return st;
+  if ((st = grow(reinterpret_cast<void**>(&b->d_q), &b->q_cap, q_bytes)) != SA_OK) return st;
+  if ((st = grow(reinterpret_cast<void**>(&b->d_out), &b->out_cap, q_bytes)) != SA_OK) return st;
+  if ((st = grow(&b->d_ws, &b->ws_cap, ws_bytes)) != SA_OK) return st;
+  SA_CUDA_TRY(cudaEventRecord(b->ev[0], b->stream));
+  SA_CUDA_TRY(cudaMemcpyAsync(b->d_kv, kv_host, kv_bytes, cudaMemcpyHostToDevice, b->stream));
+  SA_CUDA_TRY(cudaMemcpyAsync(b->d_q, query_host, q_bytes, cudaMemcpyHostToDevice, b->stream));
+  SA_CUDA_TRY(cudaEventRecord(b->ev[1], b->stream));
+  st = sa_attention_packed(static_cast<const uint16_t*>(b->d_kv), b->d_q, tokens, query_heads,
+                           kv_heads, head_dim, scale, b->d_out, 0, b->d_ws, b->ws_cap, b->stream);
+  if (st != SA_OK) return st;
+  SA_CUDA_TRY(cudaEventRecord(b->ev[2], b->stream));
+  const bool consume = (flags & SA_ATTN_CONSUME) != 0;
+  if (consume) {
+    if ((st = launch_consume(b->d_out, (int)(query_heads * head_dim), b->d_checksum, b->stream)) != SA_OK)
+      return st;
+  }
+  SA_CUDA_TRY(cudaEventRecord(b->ev[3], b->stream));
+  if (flags & (SA_ATTN_COPY_OUTPUT | SA_ATTN_CONSUME)) {
+    SA_CUDA_TRY(cudaMemcpyAsync(out_host, consume ? b->d_checksum : b->d_out,
+                                consume ? sizeof(float) : q_bytes, cudaMemcpyDeviceToHost,
+                                b->stream));
+  }
+  SA_CUDA_TRY(cudaEventRecord(b->ev[4], b->stream));
+  SA_CUDA_TRY(cudaEventSynchronize(b->ev[4]));
+  if (timings) {
+    float ms[4] = {0, 0, 0, 0};
+    for (int i = 0; i < 4; ++i) cudaEventElapsedTime(&ms[i], b->ev[i], b->ev[i + 1]);
+    timings->h2d_ms = ms[0];
+    timings->kernel_ms = ms[1];
+    timings->consumer_ms = ms[2];
+    timings->d2h_ms = ms[3];
+  }
+  return SA_OK;
+}
+
+SA_API sa_status sa_backend_execute(sa_backend* b, void* pinned_input, size_t bytes, uint8_t mask,
+                                    sa_timings* timings, uint64_t* checksum_out) {
+  if (!b || (!pinned_input && bytes)) return fail(SA_ERR_INVALID_ARG, "execute: null argument");
+  DeviceGuard guard(b->device);
+  sa_status st;
+  if ((st = grow(reinterpret_cast<void**>(&b->d_io), &b->io_cap, 2 * std::max<size_t>(bytes, 1))) != SA_OK)
+    return st;
+  std::vector<uint8_t> output(bytes);
+  uint8_t* d_in = b->d_io;
+  uint8_t* d_out = b->d_io + bytes;
+  SA_CUDA_TRY(cudaEventRecord(b->ev[0], b->stream));
+  SA_CUDA_TRY(cudaMemcpyAsync(d_in, pinned_input, bytes, cudaMemcpyHostToDevice, b->stream));
+  SA_CUDA_TRY(cudaEventRecord(b->ev[1], b->stream));
+  if ((st = launch_xor(d_in, d_out, bytes, mask, b->stream)) != SA_OK) return st;
+  SA_CUDA_TRY(cudaEventRecord(b->ev[2], b->stream));
+  SA_CUDA_TRY(cudaMemcpyAsync(output.data(), d_out, bytes, cudaMemcpyDeviceToHost, b->stream));
+  SA_CUDA_TRY(cudaEventRecord(b->ev[3], b->stream));
+  SA_CUDA_TRY(cudaEventSynchronize(b->ev[3]));
+  float ms[3] = {0, 0, 0};
+  for (int i = 0; i < 3; ++i) cudaEventElapsedTime(&ms[i], b->ev[i], b->ev[i + 1]);
+  if (timings) {
+    timings->h2d_ms = ms[0];
+    timings->kernel_ms = ms[1];
+    timings->consumer_ms = 0;
+    timings->d2h_ms = ms[2];
+  }
+  uint64_t sum = 0;
+  for (const uint8_t v : output) sum += v;
+  if (checksum_out) *checksum_out = sum;
+  return SA_OK;
+}
+
+}  // extern "C"
+
+// ================================================== paged decode context
+
+namespace {
+
+sa_status validate_config(const sa_ctx_config& c) {
+  if (c.head_dim != kHeadDim) return fail(SA_ERR_UNSUPPORTED, "ctx: head_dim must be 128");
+  if (c.query_heads <= 0 || c.kv_heads <= 0 || c.query_heads % c.kv_heads != 0)
+    return fail(SA_ERR_INVALID_ARG, "ctx: query_heads must be a positive multiple of kv_heads");
+  const int g = c.query_heads / c.kv_heads;
+  if (g != 1 && g != 2 && g != 4 && g != 8)
+    return fail(SA_ERR_UNSUPPORTED, "ctx: query heads per KV head must be 1, 2, 4 or 8");
+  if (c.layers <= 0 || c.seqs <= 0) return fail(SA_ERR_INVALID_ARG, "ctx: layers and seqs must be positive");
+  if (c.pool_blocks <= 0 || c.table_blocks <= 0)
+    return fail(SA_ERR_INVALID_ARG, "ctx: pool_blocks and table_blocks must be positive");
+  if ((int64_t)c.pool_blocks * kBlockTokens > 0x7fffffffLL)
+    return fail(SA_ERR_UNSUPPORTED, "ctx: pool too large for 32-bit rows");
+  if (c.budget_blocks <= 0 || c.init_blocks < 0 || c.local_blocks < 0 ||
+      c.init_blocks + c.local_blocks > c.budget_blocks)
+    return fail(SA_ERR_INVALID_ARG, "ctx: need budget >= init + local >= 0");
+  if (c.select_group <= 0 || c.query_heads % c.select_group != 0 || c.select_group % g != 0)
+    return fail(SA_ERR_INVALID_ARG,
+                "ctx: select_group must divide query_heads and be a multiple of query_heads/kv_heads");
+  if (c.table_blocks > select_max_blocks())
+    return fail(SA_ERR_UNSUPPORTED, "ctx: table_blocks above 16384");
+  if (c.rep_window <= 0 || c.rep_window > 64 || c.rep_topk <= 0 || c.rep_topk > kBlockTokens)
+    return fail(SA_ERR_UNSUPPORTED, "ctx: rep_window must be 1..64 and rep_topk 1..32");
+  if (!(c.scale > 0.f) || !std::isfinite(c.scale)) return fail(SA_ERR_INVALID_ARG, "ctx: bad scale");
+  return SA_OK;
+}
+
+template <class T>
+sa_status dalloc(T** p, size_t count) {
+  *p = nullptr;
+  if (count == 0) count = 1;
+  const cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(SA_ERR_NO_MEMORY, std::string("ctx: cudaMalloc failed: ") + cudaGetErrorString(e));
+  }
+  return SA_OK;
+}
+
+sa_status ctx_select(sa_ctx* c, const float* query) {
+  SelectParams p{};
+  p.query = query;
+  p.reps = c->dev.reps;
+  p.s_dim = c->table_pad;
+  p.s_block = 1;
+  p.s_head = (int64_t)kHeadDim * c->table_pad;
+  p.s_sl = (int64_t)c->cfg.query_heads * p.s_head;
+  p.qh = c->cfg.query_heads;
+  p.group = c->cfg.select_group;
+  p.n_groups = c->n_sel_groups;
+  p.d = kHeadDim;
+  p.num_sl = c->num_sl;
+  p.nb = c->dev.num_sealed;
+  p.fixed_nb = 0;
+  p.nb_cap = c->table_pad;
+  p.budget = c->cfg.budget_blocks;
+  p.init = c->cfg.init_blocks;
+  p.local = c->cfg.local_blocks;
+  p.ids = c->selected;
+  p.counts = c->selected_count;
+  p.scores = c->scores;
+  p.counters = c->select_counters;
+  p.status = c->dev.status;
+  ++c->launches;
+  return launch_select(p, c->stream);
+}
+
+sa_status ctx_attend(sa_ctx* c, const float* query, void* out) {
+  AttnParams p{};
+  p.kv_heads = c->cfg.kv_heads;
+  p.group = c->group;
+  p.num_sl = c->num_sl;
+  p.pool_blocks = c->cfg.pool_blocks;
+  p.sel_ids = c->selected;
+  p.sel_count = c->selected_count;
+  p.sel_stride = c->cfg.budget_blocks;
+  p.n_sel_groups = c->n_sel_groups;
+  p.kv_per_sel_group = c->cfg.select_group / c->group;
+  p.fixed_nsel = 0;
+  p.table = c->dev.table;
+  p.table_stride = c->cfg.table_blocks;
+  p.tail_block = c->dev.tail_block;
+  p.tail_len = c->dev.tail_len;
+  p.query = query;
+  p.out = out;
+  p.out_fp16 = c->cfg.out_fp16;
+  p.scale_log2 = c->cfg.scale * 1.4426950408889634f;
+  p.split_entries = c->attn_split_entries;
+  p.max_splits = c->attn_splits;
+  p.partial = c->attn_partial;
+  p.counters = c->attn_counters;
+  p.status = c->dev.status;
+  ++c->launches;
+  return launch_attention(p, c->pool_map, c->stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+SA_API sa_status sa_ctx_create(const sa_ctx_config* config, sa_ctx** out) {
+  if (!config || !out) return fail(SA_ERR_INVALID_ARG, "ctx: null argument");
+  *out = nullptr;
+  sa_status st = validate_config(*config);
+  if (st != SA_OK) return st;
+  DeviceGuard guard(config->device);
+  if (!guard.ok()) return fail(SA_ERR_CUDA, "ctx: cudaSetDevice failed");
+  auto* c = new (std::nothrow) sa_ctx();
+  if (!c) return fail(SA_ERR_NO_MEMORY, "ctx: allocation failed");
+  c->cfg = *config;
+  const auto& g = c->cfg;
+  c->num_sl = g.seqs * g.layers;
+  c->group = g.query_heads / g.kv_heads;
+  c->n_sel_groups = g.query_heads / g.select_group;
+  c->table_pad = (g.table_blocks + 3) & ~3;
+  c->prefilled.assign(c->num_sl, 0);
+  const size_t nsl = c->num_sl;
+  const int64_t row_elems = 2LL * g.kv_heads * kHeadDim;
+  CtxDev& d = c->dev;
+  d.row_elems = row_elems;
+  d.pool_blocks = g.pool_blocks;
+  d.table_blocks = g.table_blocks;
+  d.reps_cap = c->table_pad;
+  d.num_sl = c->num_sl;
+  d.qh = g.query_heads;
+  d.kv_heads = g.kv_heads;
+  d.rep_window = g.rep_window;
+  d.rep_topk = g.rep_topk;
+  d.rep_scale = 1.0f / std::sqrt((float)kHeadDim);
+  const int units = c->num_sl * g.kv_heads;
+  c->attn_splits = attention_plan_splits(units, g.budget_blocks + 1, &c->attn_split_entries);
+
+  st = cuda_status(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  c->own_stream = st == SA_OK;
+  // d.table_blocks is the table row stride; reps use the padded capacity.
+  if (st == SA_OK) st = dalloc(&d.pool, (size_t)g.pool_blocks * kBlockTokens * row_elems);
+  if (st == SA_OK) st = dalloc(&d.reps, nsl * g.query_heads * kHeadDim * (size_t)c->table_pad);
+  if (st == SA_OK) st = dalloc(&d.table, nsl * g.table_blocks);
+  if (st == SA_OK) st = dalloc(&d.num_sealed, nsl);
+  if (st == SA_OK) st = dalloc(&d.tail_block, nsl);
+  if (st == SA_OK) st = dalloc(&d.tail_len, nsl);
+  if (st == SA_OK) st = dalloc(&d.generation, nsl);
+  if (st == SA_OK) st = dalloc(&d.query_ring, nsl * g.query_heads * kBlockTokens * kHeadDim);
+  if (st == SA_OK) st = dalloc(&d.free_list, (size_t)g.pool_blocks);
+  if (st == SA_OK) st = dalloc(&d.free_top, 1);
+  if (st == SA_OK) st = dalloc(&d.seal_counters, 1);
+  if (st == SA_OK) st = dalloc(&d.status, 1);
+  if (st == SA_OK) st = dalloc(&c->selected, nsl * c->n_sel_groups * g.budget_blocks);
+  if (st == SA_OK) st = dalloc(&c->selected_count, nsl * c->n_sel_groups);
+  if (st == SA_OK) st = dalloc(&c->scores, nsl * c->n_sel_groups * (size_t)c->table_pad);
+  if (st == SA_OK) st = dalloc(&c->select_counters, nsl * c->n_sel_groups);
+  if (st == SA_OK)
+    st = dalloc(reinterpret_cast<char**>(&c->attn_partial),
+                attention_scratch_bytes(units, c->attn_splits, c->group));
+  if (st == SA_OK) st = dalloc(&c->attn_counters, (size_t)units);
+  if (st == SA_OK) st = dalloc(&c->d_query, nsl * g.query_heads * kHeadDim);
+  if (st == SA_OK) st = dalloc(reinterpret_cast<float**>(&c->d_kv_new), nsl * row_elems);
+  if (st == SA_OK) st = dalloc(reinterpret_cast<float**>(&c->d_out), nsl * g.query_heads * kHeadDim);
+  if (st == SA_OK)
+    st = cuda_status(cudaHostAlloc(reinterpret_cast<void**>(&c->h_status), sizeof(uint32_t),
+                                   cudaHostAllocDefault),
+                     "cudaHostAlloc status");
+  if (st == SA_OK)
+    st = make_row_tensor_map(&c->pool_map, d.pool, (uint64_t)row_elems,
+                             (uint64_t)g.pool_blocks * kBlockTokens);
+  if (st == SA_OK) {
+    SA_CUDA_TRY(cudaMemset(d.pool, 0, (size_t)g.pool_blocks * kBlockTokens * row_elems * 2));
+    SA_CUDA_TRY(cudaMemset(d.reps, 0, nsl * g.query_heads * kHeadDim * (size_t)c->table_pad * 4));
+    SA_CUDA_TRY(cudaMemset(d.seal_counters, 0, sizeof(int)));
+    SA_CUDA_TRY(cudaMemset(c->select_counters, 0, nsl * c->n_sel_groups * sizeof(int)));
+    SA_CUDA_TRY(cudaMemset(c->attn_counters, 0, (size_t)units * sizeof(int)));
+    SA_CUDA_TRY(cudaMemset(c->selected_count, 0, nsl * c->n_sel_groups * sizeof(int)));
+    st = sa_ctx_reset(c);
+  }
+  if (st != SA_OK) {
+    const std::string msg = g_last_error;
+    sa_ctx_destroy(c);
+    g_last_error = msg;
+    return st;
+  }
+  *out = c;
+  return SA_OK;
+}
+
+SA_API sa_status sa_ctx_destroy(sa_ctx* c) {
+  if (!c) return SA_OK;
+  DeviceGuard guard(c->cfg.device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  CtxDev& d = c->dev;
+  void* ptrs[] = {d.pool, d.reps, d.table, d.num_sealed, d.tail_block, d.tail_len, d.generation,
+                  d.query_ring, d.free_list, d.free_top, d.seal_counters, d.status, c->selected,
+                  c->selected_count, c->scores, c->select_counters, c->attn_partial,
+                  c->attn_counters, c->d_query, c->d_kv_new, c->d_out};
+  for (void* p : ptrs) cudaFree(p);
+  if (c->h_status) cudaFreeHost(c->h_status);
+  if (c->own_stream && c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+  return SA_OK;
+}
+
+SA_API sa_status sa_ctx_get_ptrs(sa_ctx* c, sa_ctx_ptrs* o) {
+  if (!c || !o) return fail(SA_ERR_INVALID_ARG, "ctx: null argument");
+  o->pool = c->dev.pool;
+  o->reps = c->dev.reps;
+  o->table = c->dev.table;
+  o->num_sealed = c->dev.num_sealed;
+  o->tail_block = c->dev.tail_block;
+  o->tail_len = c->dev.tail_len;
+  o->generation = c->dev.generation;
+  o->query_ring = c->dev.query_ring;
+  o->selected = c->selected;
+  o->selected_count = c->selected_count;
+  o->scores = c->scores;
+  o->free_list = c->dev.free_list;
+  o->free_top = c->dev.free_top;
+  o->status = c->dev.status;
+  return SA_OK;
+}
+
+SA_API sa_status sa_ctx_set_stream(sa_ctx* c, void* stream) {
+  if (!c) return fail(SA_ERR_INVALID_ARG, "ctx: null");
+  DeviceGuard guard(c->cfg.device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  if (c->own_stream && c->stream) cudaStreamDestroy(c->stream);
+  c->own_stream = false;
+  c->stream = static_cast<cudaStream_t>(stream);
+  return SA_OK;
+}
+
+SA_API void* sa_ctx_stream(sa_ctx* c) { return c ? static_cast<void*>(c->stream) : nullptr; }
+
+SA_API sa_status sa_ctx_reset(sa_ctx* c) {
+  if (!c) return fail(SA_ERR_INVALID_ARG, "ctx: null");
+  DeviceGuard guard(c->cfg.device);
+  const auto& g = c->cfg;
+  const size_t nsl = c->num_sl;
+  SA_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  std::vector<int32_t> free_list(g.pool_blocks);
+  for (int i = 0; i < g.pool_blocks; ++i) free_list[i] = g.pool_blocks - 1 - i;  // pops ascend
+  const int32_t top = g.pool_blocks;
+  SA_CUDA_TRY(cudaMemcpy(c->dev.free_list, free_list.data(), free_list.size() * 4, cudaMemcpyHostToDevice));
+  SA_CUDA_TRY(cudaMemcpy(c->dev.free_top, &top, 4, cudaMemcpyHostToDevice));
+  SA_CUDA_TRY(cudaMemset(c->dev.table, 0xff, nsl * g.table_blocks * 4));
+  SA_CUDA_TRY(cudaMemset(c->dev.num_sealed, 0, nsl * 4));
+  SA_CUDA_TRY(cudaMemset(c->dev.tail_block, 0xff, nsl * 4));
+  SA_CUDA_TRY(cudaMemset(c->dev.tail_len, 0, nsl * 4));
+  SA_CUDA_TRY(cudaMemset(c->dev.generation, 0, nsl * 4));
+  SA_CUDA_TRY(cudaMemset(c->dev.status, 0, 4));
+  std::fill(c->prefilled.begin(), c->prefilled.end(), 0);
+  return SA_OK;
+}
+
+SA_API sa_status sa_ctx_prefill(sa_ctx* c, int32_t seq, int32_t layer, int32_t blocks,
+                                int32_t* phys_out_host) {
+  if (!c) return fail(SA_ERR_INVALID_ARG, "ctx: null");
+  const auto& g = c->cfg;
+  if (seq < 0 || seq >= g.seqs || layer < 0 || layer >= g.layers || blocks < 0)
+    return fail(SA_ERR_INVALID_ARG, "prefill: seq/layer/blocks out of range");
+  if (blocks > g.table_blocks) return fail(SA_ERR_CAPACITY, "prefill: more blocks than table_blocks");
+  const int sl = seq * g.layers + layer;
+  if (c->prefilled[sl]) return fail(SA_ERR_INVALID_ARG, "prefill: (seq, layer) already prefilled; reset first");
+  DeviceGuard guard(g.device);
+  SA_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  int32_t top = 0;
+  SA_CUDA_TRY(cudaMemcpy(&top, c->dev.free_top, 4, cudaMemcpyDeviceToHost));
+  if (top < blocks + 1) return fail(SA_ERR_CAPACITY, "prefill: pool has too few free blocks");
+  std::vector<int32_t> slice(blocks + 1);
+  SA_CUDA_TRY(cudaMemcpy(slice.data(), c->dev.free_list + (top - blocks - 1), (blocks + 1) * 4,
+                         cudaMemcpyDeviceToHost));
+  std::vector<int32_t> phys(blocks + 1);
+  for (int i = 0; i <= blocks; ++i) phys[i] = slice[blocks - i];  // pop order
+  const int32_t new_top = top - blocks - 1;
+  const int32_t zero = 0;
+  SA_CUDA_TRY(cudaMemcpy(c->dev.free_top, &new_top, 4, cudaMemcpyHostToDevice));
+  if (blocks)
+    SA_CUDA_TRY(cudaMemcpy(c->dev.table + (size_t)sl * g.table_blocks, phys.data(), blocks * 4,
+                           cudaMemcpyHostToDevice));
+  SA_CUDA_TRY(cudaMemcpy(c->dev.num_sealed + sl, &blocks, 4, cudaMemcpyHostToDevice));
+  SA_CUDA_TRY(cudaMemcpy(c->dev.tail_block + sl, &phys[blocks], 4, cudaMemcpyHostToDevice));
+  SA_CUDA_TRY(cudaMemcpy(c->dev.tail_len + sl, &zero, 4, cudaMemcpyHostToDevice));
+  SA_CUDA_TRY(cudaMemcpy(c->dev.generation + sl, &zero, 4, cudaMemcpyHostToDevice));
+  c->prefilled[sl] = 1;
+  if (phys_out_host) std::memcpy(phys_out_host, phys.data(), (blocks + 1) * 4);
+  return SA_OK;
+}
+
+SA_API sa_status sa_ctx_build_reps(sa_ctx* c, int32_t seq, int32_t layer, int32_t first,
+                                   int32_t count, const float* prompt_queries, int32_t window,
+                                   int32_t topk, int32_t per_block) {
+  if (!c || !prompt_queries) return fail(SA_ERR_INVALID_ARG, "build_reps: null argument");
+  const auto& g = c->cfg;
+  if (seq < 0 || seq >= g.seqs || layer < 0 || layer >= g.layers || first < 0 || count < 0 ||
+      first + count > g.table_blocks)
+    return fail(SA_ERR_INVALID_ARG, "build_reps: range out of bounds");
+  if (count == 0) return SA_OK;
+  DeviceGuard guard(g.device);
+  const int sl = seq * g.layers + layer;
+  RepParams p{};
+  p.kv = c->dev.pool;
+  p.row_stride = c->dev.row_elems;
+  p.table = c->dev.table;
+  p.table_offset = sl * g.table_blocks + first;
+  p.kv_heads = g.kv_heads;
+  p.q = prompt_queries;
+  p.qh = g.query_heads;
+  p.d = kHeadDim;
+  p.tokens = count * kBlockTokens;
+  p.blocks = count;
+  p.window = window;
+  p.topk = topk;
+  p.scale = 1.0f / std::sqrt((float)kHeadDim);
+  p.values = c->dev.reps + (size_t)sl * g.query_heads * kHeadDim * c->table_pad + first;
+  p.o_head = (int64_t)kHeadDim * c->table_pad;
+  p.o_block = 1;
+  p.o_dim = c->table_pad;
+  p.offsets = nullptr;
+  p.status = c->dev.status;
+  ++c->launches;
+  return per_block ? launch_build_reps_per_block(p, c->stream) : launch_build_reps(p, c->stream);
+}
+
+SA_API sa_status sa_ctx_append(sa_ctx* c, const float* query, const void* kv_new, int32_t kv_fp32) {
+  if (!c || !query || !kv_new) return fail(SA_ERR_INVALID_ARG, "append: null argument");
+  DeviceGuard guard(c->cfg.device);
+  ++c->launches;
+  return launch_append(c->dev, query, kv_new, kv_fp32, c->stream);
+}
+
+SA_API sa_status sa_ctx_select(sa_ctx* c, const float* query) {
+  if (!c || !query) return fail(SA_ERR_INVALID_ARG, "select: null argument");
+  DeviceGuard guard(c->cfg.device);
+  return ctx_select(c, query);
+}
+
+SA_API sa_status sa_ctx_attend(sa_ctx* c, const float* query, void* out) {
+  if (!c || !query || !out) return fail(SA_ERR_INVALID_ARG, "attend: null argument");
+  DeviceGuard guard(c->cfg.device);
+  return ctx_attend(c, query, out);
+}
+
+SA_API sa_status sa_ctx_seal(sa_ctx* c) {
+  if (!c) return fail(SA_ERR_INVALID_ARG, "seal: null ctx");
+  DeviceGuard guard(c->cfg.device);
+  c->launches += 2;
+  return launch_seal(c->dev, c->stream);
+}
+
+SA_API sa_status sa_ctx_step(sa_ctx* c, const float* query, const void* kv_new, int32_t kv_fp32,
+                             void* out) {
+  if (!c || !query || !kv_new || !out) return fail(SA_ERR_INVALID_ARG, "step: null argument");
+  DeviceGuard guard(c->cfg.device);
+  sa_status st;
+  ++c->launches;
+  if ((st = launch_append(c->dev, query, kv_new, kv_fp32, c->stream)) != SA_OK) return st;
+  if ((st = ctx_select(c, query)) != SA_OK) return st;
+  if ((st = ctx_attend(c, query, out)) != SA_OK) return st;
+  c->launches += 2;
+  return launch_seal(c->dev, c->stream);
+}
+
+SA_API sa_status sa_ctx_step_host(sa_ctx* c, const float* query_host, const void* kv_new_host,
+                                  int32_t kv_fp32, void* out_host) {
+  if (!c || !query_host || !kv_new_host || !out_host)
+    return fail(SA_ERR_INVALID_ARG, "step_host: null argument");
+  DeviceGuard guard(c->cfg.device);
+  const auto& g = c->cfg;
+  const size_t q_bytes = (size_t)c->num_sl * g.query_heads * kHeadDim * sizeof(float);
+  const size_t kv_bytes = (size_t)c->num_sl * c->dev.row_elems * (kv_fp32 ? 4 : 2);
+  const size_t out_bytes = (size_t)c->num_sl * g.query_heads * kHeadDim * (g.out_fp16 ? 2 : 4);
+  SA_CUDA_TRY(cudaMemcpyAsync(c->d_query, query_host, q_bytes, cudaMemcpyHostToDevice, c->stream));
+  SA_CUDA_TRY(cudaMemcpyAsync(c->d_kv_new, kv_new_host, kv_bytes, cudaMemcpyHostToDevice, c->stream));
+  sa_status st = sa_ctx_step(c, c->d_query, c->d_kv_new, kv_fp32, c->d_out);
+  if (st != SA_OK) return st;
+  SA_CUDA_TRY(cudaMemcpyAsync(out_host, c->d_out, out_bytes, cudaMemcpyDeviceToHost, c->stream));
+  SA_CUDA_TRY(cudaMemcpyAsync(c->h_status, c->dev.status, sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                              c->stream));
+  SA_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  if (*c->h_status)
+    return fail(*c->h_status & SA_DEV_TIMEOUT ? SA_ERR_TIMEOUT : SA_ERR_DEVICE,
+                "step_host: device status bits 0x" + std::to_string(*c->h_status));
+  return SA_OK;
+}
+
+SA_API sa_status sa_ctx_sync(sa_ctx* c, uint32_t* bits_out) {
+  if (!c) return fail(SA_ERR_INVALID_ARG, "sync: null ctx");
+  DeviceGuard guard(c->cfg.device);
+  SA_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  uint32_t bits = 0;
+  SA_CUDA_TRY(cudaMemcpy(&bits, c->dev.status, sizeof(bits), cudaMemcpyDeviceToHost));
+  if (bits_out) *bits_out = bits;
+  if (bits & SA_DEV_TIMEOUT) return fail(SA_ERR_TIMEOUT, "device wait timed out");
+  if (bits) return fail(SA_ERR_DEVICE, "device status bits 0x" + std::to_string(bits));
+  return SA_OK;
+}
+
+SA_API uint64_t sa_ctx_launch_count(const sa_ctx* c) { return c ? c->launches : 0; }
+
+}  // extern "C"

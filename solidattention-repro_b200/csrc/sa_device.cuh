@@ -1,0 +1,149 @@
+// sa_device.cuh -- device-side helpers shared by the sm_100a kernels:
+// status bits, FP16 conversion, mbarrier + TMA (cp.async.bulk.tensor) wrappers
+// with bounded waits, and small block-wide scans.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "sa_b200.h"
+#include "sa_internal.h"
+
+namespace sa {
+
+// A bounded wait gives up after this many SM clock cycles (~1 s at 1.9 GHz),
+// sets SA_DEV_TIMEOUT and lets the kernel return instead of hanging.
+constexpr long long kWaitLimitCycles = 2000000000LL;
+
+__device__ __forceinline__ void raise_status(uint32_t* status, uint32_t bit) {
+  if (status) atomicOr(status, bit);
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- mbarrier ------------------------------------------------------------
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Waits for the phase with the given parity; false (and SA_DEV_TIMEOUT) if
+// it did not complete within kWaitLimitCycles.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  uint32_t* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long start = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - start > kWaitLimitCycles) {
+      raise_status(status, SA_DEV_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
+// ---- TMA -------------------------------------------------------------------
+
+// 2-D tiled load of box {x extent, y extent} at coordinates (x, y) into
+// shared memory, completing `bar`'s transaction count. No cluster multicast.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---- conversions -----------------------------------------------------------
+
+__device__ __forceinline__ float h2f(uint16_t h) {
+  return __half2float(__ushort_as_half(h));
+}
+
+__device__ __forceinline__ uint16_t f2h_rn(float f) {
+  return __half_as_ushort(__float2half_rn(f));
+}
+
+__device__ __forceinline__ float2 h2x2f(uint32_t packed) {
+  __half2 h;
+  *reinterpret_cast<uint32_t*>(&h) = packed;
+  return __half22float2(h);
+}
+
+// Order-preserving map of a float to uint32 (larger float -> larger key).
+// -0.0 is folded onto +0.0 so that the two compare equal, as `>` does.
+__device__ __forceinline__ uint32_t float_order_key(float f) {
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7fffffffu) == 0) u = 0;
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// ---- block scans -------------------------------------------------------------
+
+// Exclusive prefix sum over the threads of a block (blockDim.x <= 1024,
+// multiple of 32). `scratch` holds >= 33 ints of shared memory. Returns the
+// exclusive prefix; *total gets the block sum. Contains __syncthreads.
+__device__ __forceinline__ int block_exclusive_scan(int value, int* scratch, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int warps = blockDim.x >> 5;
+  int inclusive = value;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, inclusive, o);
+    if (lane >= o) inclusive += n;
+  }
+  if (lane == 31) scratch[warp] = inclusive;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < warps ? scratch[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += n;
+    }
+    if (lane < warps) scratch[lane] = w;  // inclusive warp sums
+    if (lane == warps - 1) scratch[32] = w;
+  }
+  __syncthreads();
+  const int before = (warp > 0 ? scratch[warp - 1] : 0) + inclusive - value;
+  *total = scratch[32];
+  __syncthreads();
+  return before;
+}
+
+}  // namespace sa

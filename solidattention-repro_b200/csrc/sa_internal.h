@@ -1,0 +1,160 @@
+// sa_internal.h -- parameter blocks and launchers shared between the kernel
+// files and the C-ABI implementation (sa_api.cu). Not installed.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "sa_b200.h"
+
+namespace sa {
+
+constexpr int kHeadDim = 128;     // head dimension of every attention kernel
+constexpr int kBlockTokens = 32;  // tokens per KV block
+
+// ---- errors ------------------------------------------------------------------
+
+// Records `message` as this thread's last error and returns `status`.
+sa_status fail(sa_status status, const std::string& message);
+// Maps a CUDA error to SA_ERR_CUDA with the call's name; SA_OK on success.
+sa_status cuda_status(cudaError_t err, const char* what);
+#define SA_CUDA_TRY(call)                                     \
+  do {                                                        \
+    const sa_status _s = ::sa::cuda_status((call), #call);    \
+    if (_s != SA_OK) return _s;                               \
+  } while (0)
+
+// Raises a kernel's dynamic shared memory limit to `bytes` once per device.
+sa_status ensure_smem_limit(const void* kernel, int bytes, int* configured_per_device);
+constexpr int kMaxDevices = 64;
+
+// ---- TMA descriptors ---------------------------------------------------------
+
+// 2-D tensor map over token rows: x = FP16 element within a row of
+// `row_elems`, y = row. Box {64 elements (128 B), 32 rows}, 128 B swizzle.
+sa_status make_row_tensor_map(CUtensorMap* map, const void* base, uint64_t row_elems,
+                              uint64_t rows);
+
+// ---- attention (sa_attention.cu) -----------------------------------------------
+
+struct AttnParams {
+  int kv_heads;          // KV heads in a pool row
+  int group;             // query heads per KV head (1, 2, 4, 8)
+  int num_sl;            // (sequence, layer) pairs
+  int pool_blocks;       // physical 32-token blocks addressable by the map
+  // selected blocks per (sl, selection group): logical ids, ascending
+  const int32_t* sel_ids;    // null -> identity 0..n-1
+  const int32_t* sel_count;  // null -> fixed_nsel
+  int sel_stride;            // ids per selection group
+  int n_sel_groups;          // selection groups per sl
+  int kv_per_sel_group;      // KV heads sharing one selection group
+  int fixed_nsel;
+  // logical -> physical block table per sl
+  const int32_t* table;  // null -> identity
+  int table_stride;
+  // open tail per sl (tail_len tokens of physical block tail_block)
+  const int32_t* tail_block;  // null -> fixed_tail_block
+  const int32_t* tail_len;    // null -> fixed_tail_len
+  int fixed_tail_block;
+  int fixed_tail_len;
+  const float* query;  // [num_sl][kv_heads*group][128]
+  void* out;           // [num_sl][kv_heads*group][128]
+  int out_fp16;
+  float scale_log2;     // softmax scale * log2(e)
+  int split_entries;    // entries (blocks) per CTA
+  int max_splits;       // grid.x
+  float* partial;       // [units][max_splits][group][2 + 128]
+  int* counters;        // [units], zero between launches
+  uint32_t* status;
+};
+
+// Entries a unit can hold at most (selected blocks + tail).
+int attention_plan_splits(int units, int max_entries, int* split_entries);
+size_t attention_scratch_bytes(int units, int max_splits, int group);
+sa_status launch_attention(const AttnParams& p, const CUtensorMap& map, cudaStream_t stream);
+
+// ---- selection (sa_select.cu) ----------------------------------------------------
+
+struct SelectParams {
+  const float* query;  // [num_sl][qh][d]
+  const float* reps;
+  int64_t s_sl, s_head, s_block, s_dim;  // element strides of reps
+  int qh, group, n_groups, d;
+  int num_sl;
+  const int32_t* nb;  // [num_sl] sealed blocks, null -> fixed_nb
+  int fixed_nb;
+  int nb_cap;         // capacity of scores rows and of reps along blocks
+  int budget, init, local;
+  int32_t* ids;       // [num_sl][n_groups][budget]
+  int32_t* counts;    // [num_sl][n_groups] (nullable)
+  float* scores;      // [num_sl][n_groups][nb_cap]
+  int* counters;      // [num_sl][n_groups], zero between launches
+  uint32_t* status;
+};
+
+int select_max_blocks();
+sa_status launch_select(const SelectParams& p, cudaStream_t stream);
+
+// ---- representatives, append, seal (sa_lifecycle.cu) ------------------------------
+
+struct RepParams {
+  // keys: row r of token p at kv + row_of(p) * row_stride + kv_head * d
+  const uint16_t* kv;
+  int64_t row_stride;       // elements between token rows
+  const int32_t* table;     // null -> row_of(p) = p; else table[table_offset + p/32]*32 + p%32
+  int table_offset;
+  int kv_heads;
+  // queries of head h, position p: q + (h * tokens + p) * d
+  const float* q;
+  int qh, d;
+  int tokens;               // tokens of one call
+  int blocks;               // tokens / 32
+  int window, topk;
+  float scale;              // 1/sqrt(d)
+  // value of (head h, block b, dim j) at values + h*o_head + b*o_block + j*o_dim
+  float* values;
+  int64_t o_head, o_block, o_dim;
+  int32_t* offsets;         // [qh][blocks][topk] (nullable)
+  uint32_t* status;
+};
+
+sa_status launch_build_reps(const RepParams& p, cudaStream_t stream);
+// Per-block variant: every block b of a range is its own 32-token call
+// (queries q + (h * blocks * 32 + b * 32 + p) * d, i.e. [qh][blocks*32][d]).
+sa_status launch_build_reps_per_block(const RepParams& p, cudaStream_t stream);
+
+struct CtxDev {
+  uint16_t* pool;
+  int64_t row_elems;   // 2 * kv_heads * 128
+  int pool_blocks;
+  float* reps;         // [num_sl][qh][128][reps_cap]
+  int reps_cap;        // table_blocks rounded up to a multiple of 4
+  int32_t* table;      // [num_sl][table_blocks]
+  int table_blocks;
+  int32_t* num_sealed;
+  int32_t* tail_block;
+  int32_t* tail_len;
+  int32_t* generation;
+  float* query_ring;   // [num_sl][qh][32][128]
+  int32_t* free_list;
+  int32_t* free_top;
+  int* seal_counters;  // [num_sl]
+  uint32_t* status;
+  int num_sl, qh, kv_heads;
+  int rep_window, rep_topk;
+  float rep_scale;
+};
+
+sa_status launch_append(const CtxDev& c, const float* query, const void* kv_new, int kv_fp32,
+                        cudaStream_t stream);
+sa_status launch_seal(const CtxDev& c, cudaStream_t stream);
+sa_status launch_pack_kv(uint16_t* packed, const float* key, const float* value,
+                         size_t token, size_t elements, cudaStream_t stream);
+sa_status launch_xor(const uint8_t* in, uint8_t* out, size_t bytes, uint8_t mask,
+                     cudaStream_t stream);
+sa_status launch_consume(const float* out, int n, float* checksum, cudaStream_t stream);
+
+}  // namespace sa

@@ -1,0 +1,254 @@
+// sa_select.cu -- InfLLM representative scoring + deterministic top-k block
+// selection for sm_100a.
+//
+// Replaces select_shared_blocks (cpp/src/selection.cpp:96-147), applied per
+// group of `group` query heads (a KV head's G heads, or all QH heads for the
+// reference's shared mode).
+//
+// Scoring keeps the reference's floating-point order exactly: per head a
+// sequential head_dim dot product with separately rounded multiply and add
+// (no FMA), divided by the group size and added to the block's score head by
+// head. Each thread owns 4 consecutive blocks, so with dimension-major
+// representatives ([head][dim][block]) a warp's loads of one dim are 512
+// contiguous bytes. Scores are therefore bit-identical to the reference's.
+//
+// Top-k: the reference forces [0, init) and the last `local` blocks, then
+// stable-sorts by descending score and fills up to the budget, returning ids
+// ascending. Equivalent here: pick the K = budget - |forced| largest
+// (score, -index) pairs among unforced blocks by an MSB-first radix select
+// on order-preserving 32-bit score keys, resolve ties at the threshold key by
+// ascending index, and compact the chosen flags in index order. The
+// last-arriving CTA of a (sequence-layer, group) does this (atomic counter,
+// no spinning), so the result never depends on CTA scheduling.
+#include <algorithm>
+
+#include "sa_device.cuh"
+#include "sa_internal.h"
+
+namespace sa {
+
+namespace {
+
+constexpr int kThreads = 128;
+constexpr int kBlocksPerThread = 4;
+constexpr int kChunk = kThreads * kBlocksPerThread;  // blocks per CTA
+constexpr int kMaxBlocks = 16384;
+constexpr unsigned kFull = 0xffffffffu;
+
+struct TopkShared {
+  int hist[256];
+  int scan[33];
+  int digit;
+  int above;
+  int last;
+};
+
+__device__ __forceinline__ float dot_step(float acc, float q, float r) {
+  return __fadd_rn(acc, __fmul_rn(q, r));
+}
+
+__global__ void __launch_bounds__(kThreads)
+    select_kernel(const SelectParams p, const int vec) {
+  extern __shared__ float qs[];  // [group][d] then [nb_cap] keys
+  __shared__ TopkShared ts;
+  const int unit = blockIdx.y;
+  const int sl = unit / p.n_groups;
+  const int g = unit - sl * p.n_groups;
+  const int nb = max(0, min(p.nb ? p.nb[sl] : p.fixed_nb, p.nb_cap));
+  const int nchunks = max(1, (nb + kChunk - 1) / kChunk);
+  if ((int)blockIdx.x >= nchunks) return;
+
+  const float* qsrc = p.query + ((size_t)sl * p.qh + (size_t)g * p.group) * p.d;
+  for (int i = threadIdx.x; i < p.group * p.d; i += kThreads) qs[i] = qsrc[i];
+  __syncthreads();
+
+  float* scores = p.scores + (size_t)unit * p.nb_cap;
+  const int b0 = blockIdx.x * kChunk + threadIdx.x * kBlocksPerThread;
+  if (b0 < nb) {
+    float score[kBlocksPerThread] = {0.f, 0.f, 0.f, 0.f};
+    const float divisor = (float)p.group;
+    for (int j = 0; j < p.group; ++j) {
+      const int h = g * p.group + j;
+      const float* rh = p.reps + (size_t)sl * p.s_sl + (size_t)h * p.s_head;
+      const float* qj = qs + j * p.d;
+      float dot[kBlocksPerThread] = {0.f, 0.f, 0.f, 0.f};
+      if (vec) {
+        const float* col = rh + b0;
+        int dd = 0;
+        for (; dd + 8 <= p.d; dd += 8) {
+          float4 r[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            r[u] = __ldg(reinterpret_cast<const float4*>(col + (size_t)(dd + u) * p.s_dim));
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const float q = qj[dd + u];
+            dot[0] = dot_step(dot[0], q, r[u].x);
+            dot[1] = dot_step(dot[1], q, r[u].y);
+            dot[2] = dot_step(dot[2], q, r[u].z);
+            dot[3] = dot_step(dot[3], q, r[u].w);
+          }
+        }
+        for (; dd < p.d; ++dd) {
+          const float4 r = __ldg(reinterpret_cast<const float4*>(col + (size_t)dd * p.s_dim));
+          const float q = qj[dd];
+          dot[0] = dot_step(dot[0], q, r.x);
+          dot[1] = dot_step(dot[1], q, r.y);
+          dot[2] = dot_step(dot[2], q, r.z);
+          dot[3] = dot_step(dot[3], q, r.w);
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < kBlocksPerThread; ++k) {
+          if (b0 + k >= nb) break;
+          const float* rb = rh + (size_t)(b0 + k) * p.s_block;
+          float acc = 0.f;
+          for (int dd = 0; dd < p.d; ++dd) acc = dot_step(acc, qj[dd], __ldg(rb + (size_t)dd * p.s_dim));
+          dot[k] = acc;
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kBlocksPerThread; ++k)
+        score[k] = __fadd_rn(score[k], __fdiv_rn(dot[k], divisor));
+    }
+#pragma unroll
+    for (int k = 0; k < kBlocksPerThread; ++k)
+      if (b0 + k < nb) scores[b0 + k] = score[k];
+  }
+
+  // ---- the last CTA of this (sl, group) selects ----
+  if (nchunks > 1) {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) ts.last = atomicAdd(&p.counters[unit], 1) == nchunks - 1;
+    __syncthreads();
+    if (!ts.last) return;
+    __threadfence();
+    if (threadIdx.x == 0) p.counters[unit] = 0;
+  } else {
+    __threadfence();
+    __syncthreads();
+  }
+
+  uint32_t* keys = reinterpret_cast<uint32_t*>(qs + p.group * p.d);
+  const int budget = min(p.budget, nb);
+  const int n_init = min(p.init, nb);
+  const int n_local = min(p.local, nb);
+  const int local_begin = nb - n_local;
+  const int n_forced = n_init + n_local - max(0, n_init - local_begin);
+  const int K = max(0, budget - n_forced);
+  auto forced = [&](int i) { return i < n_init || i >= local_begin; };
+
+  bool nan_seen = false;
+  for (int i = threadIdx.x; i < nb; i += kThreads) {
+    const float sc = __ldcg(scores + i);
+    nan_seen |= isnan(sc);
+    keys[i] = float_order_key(sc);
+  }
+  if (nan_seen) raise_status(p.status, SA_DEV_NONFINITE);
+  __syncthreads();
+
+  uint32_t prefix = 0, mask = 0;
+  int remaining = K;
+  if (K > 0) {
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      for (int i = threadIdx.x; i < 256; i += kThreads) ts.hist[i] = 0;
+      __syncthreads();
+      for (int i = threadIdx.x; i < nb; i += kThreads) {
+        if (forced(i)) continue;
+        const uint32_t k = keys[i];
+        if ((k & mask) == prefix) atomicAdd(&ts.hist[(k >> shift) & 255u], 1);
+      }
+      __syncthreads();
+      if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        int c[8];
+        int local = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          c[j] = ts.hist[255 - 8 * lane - j];
+          local += c[j];
+        }
+        int incl = local;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int v = __shfl_up_sync(kFull, incl, o);
+          if (lane >= o) incl += v;
+        }
+        const int before = incl - local;
+        if (before < remaining && remaining <= incl) {
+          int acc = before;
+          bool found = false;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if (!found && acc + c[j] >= remaining) {
+              ts.digit = 255 - 8 * lane - j;
+              ts.above = acc;
+              found = true;
+            }
+            acc += c[j];
+          }
+        }
+      }
+      __syncthreads();
+      prefix |= (uint32_t)ts.digit << shift;
+      mask |= 0xffu << shift;
+      remaining -= ts.above;
+      __syncthreads();
+    }
+  }
+  // Chosen: forced, or key above the threshold, or equal to it among the
+  // first `remaining` such blocks in index order.
+  const int per = (nb + kThreads - 1) / kThreads;
+  const int lo = min(nb, threadIdx.x * per);
+  const int hi = min(nb, lo + per);
+  int eq_local = 0;
+  if (K > 0)
+    for (int i = lo; i < hi; ++i) eq_local += (!forced(i) && keys[i] == prefix);
+  int eq_total = 0;
+  const int eq_before = block_exclusive_scan(eq_local, ts.scan, &eq_total);
+  auto chosen = [&](int i, int& eq_seen) {
+    if (forced(i)) return true;
+    if (K == 0) return false;
+    const uint32_t k = keys[i];
+    if (k > prefix) return true;
+    if (k == prefix) return eq_seen++ < remaining;
+    return false;
+  };
+  int cnt = 0;
+  int eq_seen = eq_before;
+  for (int i = lo; i < hi; ++i) cnt += chosen(i, eq_seen);
+  int total = 0;
+  int pos = block_exclusive_scan(cnt, ts.scan, &total);
+  int32_t* ids = p.ids + (size_t)unit * p.budget;
+  eq_seen = eq_before;
+  for (int i = lo; i < hi; ++i)
+    if (chosen(i, eq_seen) && pos < p.budget) ids[pos++] = i;
+  if (threadIdx.x == 0 && p.counts) p.counts[unit] = min(total, p.budget);
+}
+
+}  // namespace
+
+int select_max_blocks() { return kMaxBlocks; }
+
+sa_status launch_select(const SelectParams& p, cudaStream_t stream) {
+  if (p.num_sl <= 0 || p.n_groups <= 0) return SA_OK;
+  if (p.nb_cap > kMaxBlocks)
+    return fail(SA_ERR_UNSUPPORTED, "select: more than 16384 candidate blocks");
+  if ((size_t)p.num_sl * p.n_groups > 65535u)
+    return fail(SA_ERR_UNSUPPORTED, "select: more than 65535 (sequence-layer, group) units");
+  const int vec = p.s_block == 1 && p.s_dim % 4 == 0 && p.s_head % 4 == 0 && p.s_sl % 4 == 0 &&
+                  p.nb_cap % 4 == 0 && (reinterpret_cast<uintptr_t>(p.reps) & 15u) == 0;
+  const size_t smem = ((size_t)p.group * p.d + (size_t)p.nb_cap) * sizeof(float);
+  static int configured[kMaxDevices];
+  const sa_status st =
+      ensure_smem_limit((const void*)select_kernel, (int)std::max<size_t>(smem, 48 * 1024), configured);
+  if (st != SA_OK) return st;
+  const int nchunks = std::max(1, (p.nb_cap + kChunk - 1) / kChunk);
+  const dim3 grid(nchunks, p.num_sl * p.n_groups);
+  select_kernel<<<grid, kThreads, smem, stream>>>(p, vec);
+  return cuda_status(cudaGetLastError(), "select_kernel launch");
+}
+
+}  // namespace sa

@@ -1,0 +1,180 @@
+"""GPU parity of the paged decode context: append -> select -> attend -> seal.
+
+Each decode step is checked against the CPU oracle run on the context's own
+state (pool bytes, block tables and representatives copied back), so the
+comparison isolates the device path:
+* selected ids: identical to the reference selector per KV head;
+* attention: FP32 max-abs <= 2e-5 / cosine >= 0.999999 (FP16 output: 2e-3 /
+  0.99999) against the reference attention over the gathered blocks + tail;
+* seal: the tail block moves into the table unchanged, the new block's
+  representative equals the reference's build over the tail's 32 queries
+  (offsets exact up to received-mass near-ties), generation and free list
+  advance.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import cosine
+
+pytestmark = pytest.mark.gpu
+
+D = 128
+
+
+def _oracle_step(port, pool, table, nb, reps, q, tail_phys, tail_len, qh, kh, budget, init,
+                 local, scale):
+    """Reference selection per KV head + attention over gathered blocks and tail."""
+    grp = qh // kh
+    reps_ref = np.ascontiguousarray(np.transpose(reps[:, :, :nb], (0, 2, 1)))  # [qh][nb][d]
+    eff_budget = min(budget, nb)
+    ids = np.zeros((kh, eff_budget), np.int64)
+    if nb > 0:
+        ids, _ = port.select_grouped(q, reps_ref, qh, grp, nb, D, eff_budget,
+                                     min(init, eff_budget), min(local, max(0, eff_budget - min(init, eff_budget))))
+    out = np.zeros((qh, D), np.float32)
+    for h in range(kh):
+        rows = [pool[table[b]][:, :, h] for b in ids[h]] if nb > 0 else []
+        rows.append(pool[tail_phys][:tail_len, :, h])
+        packed = np.ascontiguousarray(np.concatenate(rows)).reshape(-1)
+        tokens = len(rows[:-1]) * 32 + tail_len
+        out[h * grp:(h + 1) * grp] = port.attention(packed, q[h * grp:(h + 1) * grp], tokens, grp,
+                                                    1, D, scale)
+    return ids, out
+
+
+def _reps_oracle(port, q_ring, kv_block, qh, kh, window=32, topk=4):
+    vals = np.zeros(qh * D, np.float32)
+    offs = np.zeros(qh * topk, np.int64)
+    received = np.zeros(qh * 32, np.float32)
+    port.lib.sao_build_representatives.argtypes = [C.c_void_p] * 2 + [C.c_size_t] * 7 + [C.c_void_p] * 3
+    assert port.lib.sao_build_representatives(
+        np.ascontiguousarray(q_ring).ctypes.data, np.ascontiguousarray(kv_block).ctypes.data, 32, qh,
+        kh, D, 32, window, topk, vals.ctypes.data, offs.ctypes.data, received.ctypes.data) == 0
+    return vals.reshape(qh, D), offs.reshape(qh, topk), received.reshape(qh, 32)
+
+
+@pytest.mark.parametrize("qh,kh,out_fp16", [(8, 2, False), (16, 8, True), (4, 4, False)])
+def test_decode_steps_with_seal_match_oracle(pkg, port, cuda, qh, kh, out_fp16):
+    layers, seqs, nb0, budget, init, local = 2, 2, 40, 10, 1, 2
+    steps = 36  # the 32nd step fills the tail and seals it
+    rng = np.random.default_rng(qh * 100 + kh)
+    g = torch.Generator().manual_seed(qh + kh)
+    ctx = pkg.DecodeContext(query_heads=qh, kv_heads=kh, layers=layers, seqs=seqs,
+                            pool_blocks=seqs * layers * (nb0 + 4), table_blocks=nb0 + 4,
+                            budget_blocks=budget, init_blocks=init, local_blocks=local,
+                            out_fp16=out_fp16, device=cuda)
+    for s in range(seqs):
+        for l in range(layers):
+            phys = ctx.prefill(s, l, nb0)
+            idx = torch.as_tensor(phys[:nb0], dtype=torch.long, device=cuda)
+            ctx.pool[idx] = torch.randn(nb0, 32, 2, kh, D, generator=g).half().to(cuda)
+            pq = torch.randn(qh, nb0 * 32, D, generator=g).half().float().to(cuda)
+            ctx.build_reps(s, l, 0, nb0, pq)
+    ctx.sync()
+    scale = np.float32(1) / np.sqrt(np.float32(D))
+    tol = (2e-3, 0.99999) if out_fp16 else (2e-5, 0.999999)
+    for step in range(steps):
+        q = (rng.standard_normal((seqs, layers, qh, D), dtype=np.float32)).astype(np.float16).astype(np.float32)
+        kvn = rng.standard_normal((seqs, layers, 2, kh, D), dtype=np.float32).astype(np.float16)
+        nb_before = ctx.num_sealed.cpu().numpy().copy()
+        tail_before = ctx.tail_block.cpu().numpy().copy()
+        out = ctx.step(torch.from_numpy(q).to(cuda), torch.from_numpy(kvn).to(cuda))
+        ctx.sync()
+        pool = ctx.pool.cpu().numpy().view(np.uint16)
+        table = ctx.table.cpu().numpy()
+        reps = ctx.reps.cpu().numpy()
+        sel = ctx.selected.cpu().numpy()
+        got = out.float().cpu().numpy()
+        for s in range(seqs):
+            for l in range(layers):
+                sl = s * layers + l
+                tail_len = step % 32 + 1
+                ids, want = _oracle_step(port, pool, table[sl], nb_before[sl], reps[sl],
+                                         q[s, l], tail_before[sl], tail_len, qh, kh, budget,
+                                         init, local, scale)
+                assert np.array_equal(sel[sl][:, :ids.shape[1]], ids), (step, s, l)
+                err = np.abs(got[s, l] - want).max()
+                assert err <= tol[0] and cosine(got[s, l], want) >= tol[1], (step, s, l, err)
+        if step == 31:  # sealed this step
+            nb_after = ctx.num_sealed.cpu().numpy()
+            assert (nb_after == nb_before + 1).all()
+            assert (ctx.tail_len.cpu().numpy() == 0).all()
+            assert (ctx.generation.cpu().numpy() == 1).all()
+            new_tails = ctx.tail_block.cpu().numpy()
+            assert len(set(new_tails.tolist()) | set(table[:, :nb0].ravel().tolist())) == \
+                len(new_tails) + table[:, :nb0].size
+            ring = ctx.query_ring.cpu().numpy()
+            for sl in range(seqs * layers):
+                assert table[sl, nb_before[sl]] == tail_before[sl]
+                blk = pool[tail_before[sl]].reshape(-1)
+                v, o, received = _reps_oracle(port, ring[sl], blk, qh, kh)
+                got_v = reps[sl][:, :, nb_before[sl]]
+                for h in range(qh):
+                    mass = received[h]
+                    if np.abs(got_v[h] - v[h]).max() > 1e-6:
+                        # allowed only for a received-mass near-tie at the top-4 boundary
+                        srt = np.sort(mass)[::-1]
+                        assert abs(srt[3] - srt[4]) <= 1e-6 * max(1.0, abs(srt[3])), (sl, h)
+    ctx.close()
+
+
+def test_lifecycle_bytes_follow_reference_formula(pkg, port, cuda):
+    """Token rows appended with the reference's synthetic byte formula
+    (cpp/src/kv_lifecycle_main.cpp:34-35) are sealed into blocks whose bytes
+    equal the reference's sealed store blocks; 31 tail tokens do not seal,
+    the 32nd does; generation counts seals."""
+    layers, qh, kh = 4, 16, 8
+    tv = 2 * kh * D
+    decode = 160
+    ctx = pkg.DecodeContext(query_heads=qh, kv_heads=kh, layers=layers, seqs=1,
+                            pool_blocks=layers * 8, table_blocks=8, budget_blocks=4,
+                            init_blocks=1, local_blocks=1, device=cuda)
+    for l in range(layers):
+        ctx.prefill(0, l, 0)
+    q = torch.zeros(1, layers, qh, D, device=cuda)
+    for token in range(decode):
+        vals = np.array([[(l * 1009 + token * 37 + v * 13) & 0xFFFF for v in range(tv)]
+                         for l in range(layers)], np.uint16)
+        ctx.step(q, torch.from_numpy(vals.view(np.int16)).to(cuda).view(1, layers, 2, kh, D))
+        if token == 30:
+            assert (ctx.num_sealed.cpu().numpy() == 0).all()
+            assert (ctx.tail_len.cpu().numpy() == 31).all()
+        if token == 31:
+            assert (ctx.num_sealed.cpu().numpy() == 1).all()
+            assert (ctx.tail_len.cpu().numpy() == 0).all()
+    # the formula's bit patterns include FP16 NaNs, so only that bit may be set
+    assert ctx.status_bits() & ~pkg.SA_DEV_NONFINITE == 0
+    res = port.lifecycle_run(layers, qh, kh, D, 32, 32, decode, 0, with_store=True)
+    store = res["store"].reshape(layers, res["capacity_blocks"], 32, tv)
+    pool = ctx.pool.cpu().numpy().view(np.uint16).reshape(-1, 32, tv)
+    table = ctx.table.cpu().numpy()
+    nb = ctx.num_sealed.cpu().numpy()
+    gen = ctx.generation.cpu().numpy()
+    assert (nb == decode // 32).all() and (gen == decode // 32).all()
+    # the reference keeps 32 local tokens unsealed: its sealed blocks are our first ones
+    for l in range(layers):
+        for b in range(res["sealed_total"] // layers):
+            assert np.array_equal(pool[table[l, b]], store[l, b]), (l, b)
+    ctx.close()
+
+
+def test_pool_exhaustion_sets_status_not_fault(pkg, cuda):
+    ctx = pkg.DecodeContext(query_heads=4, kv_heads=4, layers=1, seqs=1, pool_blocks=2,
+                            table_blocks=8, budget_blocks=2, init_blocks=0, local_blocks=1,
+                            device=cuda)
+    ctx.prefill(0, 0, 0)  # takes 1 block as the tail, 1 left free
+    q = torch.zeros(1, 1, 4, D, device=cuda)
+    kv = torch.zeros(1, 1, 2, 4, D, dtype=torch.float16, device=cuda)
+    for _ in range(65):  # two seals wanted, one possible; the 65th append finds a full tail
+        ctx.step(q, kv)
+    bits = ctx.status_bits()
+    assert bits & pkg.SA_DEV_POOL_EMPTY
+    assert bits & pkg.SA_DEV_TAIL_FULL
+    with pytest.raises(pkg.SparseKVError):
+        ctx.sync()
+    ctx.close()
