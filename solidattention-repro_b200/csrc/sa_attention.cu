@@ -8,22 +8,30 @@
 // Work unit: one (sequence-layer, KV head). Its token set is a list of
 // entries: the selected sealed blocks (logical ids -> physical pool blocks
 // through the block table) followed by the open tail (tail_len tokens).
-// A CTA takes `split_entries` consecutive entries of one unit.
+// A CTA takes `split_entries` consecutive entries of one unit; their
+// (physical block, token count) pairs are resolved once, in parallel, into
+// shared memory.
 //
-// Data path per entry (one KV head of one 32-token block = 16 KB):
-//   thread 0 issues four TMA tile loads (K lo/hi, V lo/hi: 32 rows x 128 B,
-//   128 B swizzle) into a 4-stage ring guarded by mbarriers;
-//   QK:  warp w owns head dims [16w, 16w+16), lane = token; q lives in
-//        registers, K is read from swizzled smem conflict-free; packed
-//        __ffma2_rn accumulates, partial logits go to smem;
-//   softmax: warp w owns tokens [4w, 4w+4); it sums the 8 partials, keeps a
-//        running max / sum per head (FP32, exp2 domain) -- an online softmax
-//        per warp over its token subset;
-//   PV:  lane owns dims [4 lane, 4 lane + 4) of the warp's tokens.
-// At the end the 8 warp states are merged by log-sum-exp; with several
-// splits per unit every CTA writes a partial (m, l, o[128]) and the last CTA
-// to arrive (atomic counter, no spinning) merges them in split order, so
-// results do not depend on CTA timing.
+// Pipeline: a stage holds two entries (2 x 16 KB: K lo/hi and V lo/hi of the
+// unit's KV head, 32 rows x 128 B per sub-tile, 128 B TMA swizzle) in a ring
+// of three stages. A stage's TMA loads complete a "full" mbarrier (bounded
+// waits); the last of the eight warps to release a stage (a shared-memory
+// arrival counter) issues the loads that refill it, so no warp ever blocks
+// on a producer.
+//
+// Consumer warp w, per stage: half-warp h takes entry h of the stage and its
+// tokens [4w, 4w+4); lane l covers head dims [8(l%16), 8(l%16)+8). Each row is
+// read as one conflict-free 128-bit swizzled shared load. QK uses packed FP32
+// FMA (__ffma2_rn) with the softmax scale folded into q, then a 16-lane
+// transpose-reduce leaves one (token, head) logit per lane. The warp keeps an
+// FP32 online softmax per head (exp2 domain, running max shared by both
+// half-warps) and skips the accumulator rescale when no running max moved.
+// At the end the warps merge by log-sum-exp; with several splits per unit
+// each CTA writes a partial (m, l, o[128]) and the last CTA to arrive (atomic
+// counter, no spinning) merges them in split order, so the result does not
+// depend on CTA timing.
+#include <algorithm>
+
 #include "sa_device.cuh"
 #include "sa_internal.h"
 
@@ -31,23 +39,29 @@ namespace sa {
 
 namespace {
 
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
-constexpr int kStages = 4;
-constexpr int kSubTile = kBlockTokens * 128;  // 32 rows x 128 B
-constexpr int kTileBytes = 4 * kSubTile;     // K lo, K hi, V lo, V hi
-constexpr int kPartialStride = 2 + kHeadDim; // m, l, o[128]
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads = kConsumerWarps * 32;
+constexpr int kStages = 3;
+constexpr int kSubTile = kBlockTokens * 128;      // 32 rows x 128 B
+constexpr int kEntryBytes = 4 * kSubTile;        // K lo, K hi, V lo, V hi
+constexpr int kStageBytes = 2 * kEntryBytes;     // two entries per stage
+constexpr int kPartialStride = 2 + kHeadDim;     // m, l, o[128]
+constexpr int kMaxSplitEntries = 64;
 constexpr unsigned kFull = 0xffffffffu;
 
 template <int G>
 struct alignas(1024) AttnSmem {
-  uint8_t tiles[kStages][kTileBytes];
-  float plog[2][kWarps][kBlockTokens][G];
-  float pw[kWarps][4][G];
-  float aw[kWarps][G];
-  float wscale[kWarps][G];
+  uint8_t tiles[kStages][kStageBytes];
+  float pbuf[kConsumerWarps][2][4][G];  // probabilities [half][token][head]
+  float abuf[kConsumerWarps][G];        // rescale factor per head
+  float wscale[kConsumerWarps][G];
+  float cta_m[G];
+  float cta_l[G];
+  int ent_phys[kMaxSplitEntries];
+  int ent_ntok[kMaxSplitEntries];
   uint64_t full[kStages];
-  int ntok[kStages];
+  int released[kStages];      // warps done with the stage's current contents
+  int stage_issues[kStages];  // loads issued into the stage so far
   int abort_flag;
   int last_flag;
 };
@@ -61,7 +75,8 @@ __device__ __forceinline__ Entry unit_entry(const AttnParams& p, int sl, int sgr
                                             int tail_len, int e) {
   Entry r;
   if (e < nsel) {
-    int logical = p.sel_ids ? p.sel_ids[(sl * p.n_sel_groups + sgroup) * p.sel_stride + e] : e;
+    const int logical =
+        p.sel_ids ? p.sel_ids[(sl * p.n_sel_groups + sgroup) * p.sel_stride + e] : e;
     if (p.table) {
       if (logical < 0 || logical >= p.table_stride) {
         raise_status(p.status, SA_DEV_BAD_BLOCK);
@@ -83,23 +98,78 @@ __device__ __forceinline__ Entry unit_entry(const AttnParams& p, int sl, int sgr
   return r;
 }
 
-// One lane's G partial logits as the widest conflict-free stores.
-template <int G>
-__device__ __forceinline__ void store_partials(float* dst, const float (&v)[G]) {
-  if constexpr (G == 1) {
-    dst[0] = v[0];
-  } else if constexpr (G == 2) {
-    *reinterpret_cast<float2*>(dst) = make_float2(v[0], v[1]);
-  } else {
+// The hardware base-2 exponential (ex2.approx, ~2 ulp).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// In-warp transpose-reduce step chain: M values per lane, halving at lane
+// offset OFF, then OFF/2, ...; a lane keeps the lower half of its values when
+// its OFF bit is clear (the upper half otherwise) and adds the partner's copy.
+template <int M, int OFF>
+struct Halve {
+  __device__ __forceinline__ static void run(float* a, int lane) {
+    if constexpr (M > 1 && OFF >= 1) {
+      const bool upper = (lane & OFF) != 0;
 #pragma unroll
-    for (int g = 0; g < G; g += 4)
-      *reinterpret_cast<float4*>(dst + g) = make_float4(v[g], v[g + 1], v[g + 2], v[g + 3]);
+      for (int j = 0; j < M / 2; ++j) {
+        const float keep = upper ? a[j + M / 2] : a[j];
+        const float send = upper ? a[j] : a[j + M / 2];
+        a[j] = keep + __shfl_xor_sync(kFull, send, OFF);
+      }
+      Halve<M / 2, OFF / 2>::run(a, lane);
+    }
   }
+};
+
+// Row read of 8 halves (16 B) of token t for a lane at dim-chunk c of a
+// swizzled 32 x 128 B sub-tile.
+__device__ __forceinline__ uint4 row8(const uint8_t* sub, int t, int c) {
+  return *reinterpret_cast<const uint4*>(sub + t * 128 + ((c ^ (t & 7)) << 4));
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float2 (&f)[4]) {
+  f[0] = h2x2f(u.x);
+  f[1] = h2x2f(u.y);
+  f[2] = h2x2f(u.z);
+  f[3] = h2x2f(u.w);
+}
+
+// Issues the TMA loads of stage j (entries 2j, 2j+1 of the CTA's range).
+template <int G>
+__device__ __forceinline__ void issue_stage(AttnSmem<G>& s, const CUtensorMap* map, int kv_heads,
+                                            int kvh, int n, int j) {
+  const int stage = j % kStages;
+  const int x = kvh * kHeadDim;
+  const int xv = kv_heads * kHeadDim + x;
+  uint32_t tx = 0;
+  for (int e = 2 * j; e < min(n, 2 * j + 2); ++e) tx += s.ent_ntok[e] > 0 ? kEntryBytes : 0;
+  if (tx) {
+    mbar_arrive_expect_tx(&s.full[stage], tx);
+    for (int e = 2 * j; e < min(n, 2 * j + 2); ++e) {
+      if (s.ent_ntok[e] <= 0) continue;
+      const int y = s.ent_phys[e] * kBlockTokens;
+      uint8_t* dst = s.tiles[stage] + (e & 1) * kEntryBytes;
+      tma_load_2d(dst, map, &s.full[stage], x, y);
+      tma_load_2d(dst + kSubTile, map, &s.full[stage], x + 64, y);
+      tma_load_2d(dst + 2 * kSubTile, map, &s.full[stage], xv, y);
+      tma_load_2d(dst + 3 * kSubTile, map, &s.full[stage], xv + 64, y);
+    }
+  } else {
+    mbar_arrive(&s.full[stage]);
+  }
+  s.stage_issues[stage] += 1;
 }
 
 template <int G>
 __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
     attention_kernel(const __grid_constant__ CUtensorMap map, const AttnParams p) {
+  // Pairs (token, head) per half-warp: 4G over 16 lanes -> VPL per lane.
+  constexpr int NPH = 4 * G;
+  constexpr int VPL = NPH > 16 ? NPH / 16 : 1;
+  constexpr int kPairShift = NPH >= 16 ? 0 : (NPH == 8 ? 1 : 2);  // lanes per pair = 1 << shift
   extern __shared__ uint8_t smem_raw[];
   AttnSmem<G>& s = *reinterpret_cast<AttnSmem<G>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -120,192 +190,235 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
   const int nsplit = max(1, (entries + p.split_entries - 1) / p.split_entries);
   if (split >= nsplit) return;
   const int e_begin = split * p.split_entries;
-  const int n = max(0, min(entries, e_begin + p.split_entries) - e_begin);
-
-  int issued = 0;  // meaningful in thread 0 only
-  auto issue = [&](int i) {
-    const int stage = i % kStages;
-    const Entry en = unit_entry(p, sl, sgroup, nsel, tail_len, e_begin + i);
-    s.ntok[stage] = en.ntok;
-    if (en.ntok > 0) {
-      mbar_arrive_expect_tx(&s.full[stage], kTileBytes);
-      const int x = kvh * kHeadDim;
-      const int xv = p.kv_heads * kHeadDim + x;
-      const int y = en.phys * kBlockTokens;
-      uint8_t* dst = s.tiles[stage];
-      tma_load_2d(dst, &map, &s.full[stage], x, y);
-      tma_load_2d(dst + kSubTile, &map, &s.full[stage], x + 64, y);
-      tma_load_2d(dst + 2 * kSubTile, &map, &s.full[stage], xv, y);
-      tma_load_2d(dst + 3 * kSubTile, &map, &s.full[stage], xv + 64, y);
-    } else {
-      mbar_arrive(&s.full[stage]);
-    }
-    issued = i + 1;
-  };
+  const int n = max(0, min(min(entries, e_begin + p.split_entries) - e_begin, kMaxSplitEntries));
+  const int nstages = (n + 1) / 2;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; ++i) mbar_init(&s.full[i], 1);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&s.full[i], 1);
+      s.released[i] = 0;
+      s.stage_issues[i] = 0;
+    }
     s.abort_flag = 0;
     mbar_fence_init();
     tma_prefetch_desc(&map);
   }
-  __syncthreads();
-  if (threadIdx.x == 0)
-    for (int i = 0; i < min(kStages, n); ++i) issue(i);
-
-  // q slice for QK: dims [16 warp, 16 warp + 16) of the unit's G heads.
-  const float* qbase = p.query + ((size_t)sl * p.kv_heads * G + (size_t)kvh * G) * kHeadDim;
-  float2 q2[G][8];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    const float4* src = reinterpret_cast<const float4*>(qbase + g * kHeadDim + 16 * warp);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float4 v = __ldg(src + i);
-      q2[g][2 * i] = make_float2(v.x, v.y);
-      q2[g][2 * i + 1] = make_float2(v.z, v.w);
-    }
+  for (int i = threadIdx.x; i < n; i += kThreads) {
+    const Entry en = unit_entry(p, sl, sgroup, nsel, tail_len, e_begin + i);
+    s.ent_phys[i] = en.phys;
+    s.ent_ntok[i] = en.ntok;
   }
+  __syncthreads();
 
-  const int kd_half = warp >> 2;
-  const int kd_chunk = (warp & 3) * 2;
-  const int pv_half = lane >> 4;
-  const int pv_chunk = (lane & 15) >> 1;
-  const int pv_sub = (lane & 1) * 8;
-  const int sm_t = lane / G;  // softmax pair (token index in warp, head)
-  const int sm_g = lane % G;
-  const bool sm_active = lane < 4 * G;
+  const int half = lane >> 4;      // which entry of the stage
+  const int l16 = lane & 15;
+  const int sub_hi = l16 >> 3;     // dims [0,64) or [64,128)
+  const int chunk = l16 & 7;       // 16 B chunk inside the 128 B row
+  const int t0 = 4 * warp;
 
-  float acc[G][4];
+  float m_run[VPL], l_run[VPL];
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    m_run[j] = -INFINITY;
+    l_run[j] = 0.f;
+  }
+  float2 acc[G][4];
 #pragma unroll
   for (int g = 0; g < G; ++g)
 #pragma unroll
-    for (int c = 0; c < 4; ++c) acc[g][c] = 0.f;
-  float m_run = -INFINITY;
-  float l_run = 0.f;
-  int consumed = 0;
+    for (int c = 0; c < 4; ++c) acc[g][c] = make_float2(0.f, 0.f);
 
-  for (int i = 0; i < n; ++i) {
-    const int stage = i % kStages;
-    if (!mbar_wait_bounded(&s.full[stage], (i / kStages) & 1, p.status)) s.abort_flag = 1;
-    const uint8_t* tile = s.tiles[stage];
-    const int ntok = s.ntok[stage];
-
-    // ---- QK partial dot products (lane = token) ----
+  if (threadIdx.x == 0)
+    for (int j = 0; j < min(kStages, nstages); ++j) issue_stage(s, &map, p.kv_heads, kvh, n, j);
+  {
+    // ---------------- every warp consumes ----------------
+    // q of this lane's 8 dims for the unit's G heads, pre-scaled into the
+    // exp2 domain.
+    float2 q[G][4];
     {
-      const uint8_t* row = tile + kd_half * kSubTile + lane * 128;
-      const int sw = lane & 7;
-      const uint4 c0 = *reinterpret_cast<const uint4*>(row + ((kd_chunk ^ sw) << 4));
-      const uint4 c1 = *reinterpret_cast<const uint4*>(row + (((kd_chunk + 1) ^ sw) << 4));
-      float2 k[8];
-      k[0] = h2x2f(c0.x); k[1] = h2x2f(c0.y); k[2] = h2x2f(c0.z); k[3] = h2x2f(c0.w);
-      k[4] = h2x2f(c1.x); k[5] = h2x2f(c1.y); k[6] = h2x2f(c1.z); k[7] = h2x2f(c1.w);
-      float part[G];
+      const float* qbase = p.query + ((size_t)sl * p.kv_heads * G + (size_t)kvh * G) * kHeadDim +
+                           8 * l16;
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        float2 a = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) a = __ffma2_rn(q2[g][j], k[j], a);
-        part[g] = a.x + a.y;
-      }
-      store_partials<G>(&s.plog[i & 1][warp][lane][0], part);
-    }
-    __syncthreads();
-    if (s.abort_flag) break;
-    consumed = i + 1;
-    // Every warp is past its PV of entry i-1: its stage can be refilled.
-    if (threadIdx.x == 0 && i >= 1 && i - 1 + kStages < n) issue(i - 1 + kStages);
-
-    // ---- online softmax over this warp's 4 tokens ----
-    float x = -INFINITY;
-    if (sm_active) {
-      const int t = 4 * warp + sm_t;
-      if (t < ntok) {
-        float sum = 0.f;
-#pragma unroll
-        for (int w2 = 0; w2 < kWarps; ++w2) sum += s.plog[i & 1][w2][t][sm_g];
-        x = sum * p.scale_log2;
+        const float4 a = __ldg(reinterpret_cast<const float4*>(qbase + g * kHeadDim));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(qbase + g * kHeadDim + 4));
+        q[g][0] = make_float2(a.x * p.scale_log2, a.y * p.scale_log2);
+        q[g][1] = make_float2(a.z * p.scale_log2, a.w * p.scale_log2);
+        q[g][2] = make_float2(b.x * p.scale_log2, b.y * p.scale_log2);
+        q[g][3] = make_float2(b.z * p.scale_log2, b.w * p.scale_log2);
       }
     }
-    float bm = fmaxf(x, __shfl_xor_sync(kFull, x, G));
-    bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 2 * G));
-    const float m_new = fmaxf(m_run, bm);
-    float alpha = 1.f, pr = 0.f;
-    if (m_new != -INFINITY) {
-      alpha = exp2f(m_run - m_new);
-      pr = exp2f(x - m_new);
-    }
-    m_run = m_new;
-    l_run = l_run * alpha + pr;
-    if (sm_active) s.pw[warp][sm_t][sm_g] = pr;
-    if (lane < G) s.aw[warp][lane] = alpha;
-    __syncwarp();
 
-    // ---- PV over the warp's tokens (lane = 4 dims) ----
+    for (int j = 0; j < nstages; ++j) {
+      const int stage = j % kStages;
+      if (*reinterpret_cast<volatile int*>(&s.abort_flag)) break;
+      if (!mbar_wait_bounded(&s.full[stage], (j / kStages) & 1, p.status)) {
+        atomicExch(&s.abort_flag, 1);
+        break;
+      }
+      const int e = 2 * j + half;
+      const int ntok = e < n ? s.ent_ntok[e] : 0;
+      const int e_other = 2 * j + (half ^ 1);
+      const int ntok_other = e_other < n ? s.ent_ntok[e_other] : 0;
+      if (t0 < ntok || t0 < ntok_other) {
+        const uint8_t* tile = s.tiles[stage] + half * kEntryBytes;
+        const uint8_t* ksub = tile + sub_hi * kSubTile;
+        const uint8_t* vsub = tile + (2 + sub_hi) * kSubTile;
+        // ---- QK over this lane's 8 dims, 4 tokens x G heads ----
+        float part[NPH];
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float a = s.aw[warp][g];
+        for (int tt = 0; tt < 4; ++tt) {
+          float2 k[4];
+          unpack8(row8(ksub, t0 + tt, chunk), k);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) acc[g][c] *= a;
-    }
+          for (int g = 0; g < G; ++g) {
+            float2 a = __fmul2_rn(q[g][0], k[0]);
+            a = __ffma2_rn(q[g][1], k[1], a);
+            a = __ffma2_rn(q[g][2], k[2], a);
+            a = __ffma2_rn(q[g][3], k[3], a);
+            part[tt * G + g] = a.x + a.y;
+          }
+        }
+        // 16-lane transpose-reduce: lane keeps VPL logits of pairs
+        // v = ((l16 >> kPairShift) * VPL + i) = (token tt, head g) as tt * G + g.
+        Halve<NPH, 8>::run(part, lane);
+        if constexpr (NPH < 16) {
 #pragma unroll
-    for (int tt = 0; tt < 4; ++tt) {
-      const int t = 4 * warp + tt;
-      if (t < ntok) {
-        const uint8_t* vrow = tile + (2 + pv_half) * kSubTile + t * 128;
-        const uint2 v = *reinterpret_cast<const uint2*>(vrow + ((pv_chunk ^ (t & 7)) << 4) + pv_sub);
-        const float2 v01 = h2x2f(v.x);
-        const float2 v23 = h2x2f(v.y);
+          for (int off = 1 << (kPairShift - 1); off >= 1; off >>= 1)
+            part[0] += __shfl_xor_sync(kFull, part[0], off);
+        }
+        // ---- online softmax: 8 tokens (4 per half-warp) per head ----
+        float pr[VPL], alpha[VPL];
+        bool moved = false;
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const float pg = s.pw[warp][tt][g];
-          const float2 pp = make_float2(pg, pg);
-          const float2 a01 = __ffma2_rn(pp, v01, make_float2(acc[g][0], acc[g][1]));
-          const float2 a23 = __ffma2_rn(pp, v23, make_float2(acc[g][2], acc[g][3]));
-          acc[g][0] = a01.x; acc[g][1] = a01.y; acc[g][2] = a23.x; acc[g][3] = a23.y;
+        for (int i = 0; i < VPL; ++i) {
+          const int v = (l16 >> kPairShift) * VPL + i;
+          const int tt = v / G;
+          const float x = (t0 + tt < ntok) ? part[i] : -INFINITY;
+          float bm = fmaxf(x, __shfl_xor_sync(kFull, x, 4));
+          bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 8));
+          bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 16));
+          const float m_new = fmaxf(m_run[i], bm);
+          alpha[i] = 1.f;
+          pr[i] = 0.f;
+          if (m_new != -INFINITY) {
+            alpha[i] = fast_exp2(m_run[i] - m_new);
+            pr[i] = fast_exp2(x - m_new);
+          }
+          moved |= m_new != m_run[i];
+          m_run[i] = m_new;
+          l_run[i] = l_run[i] * alpha[i] + pr[i];
+        }
+        if ((l16 & ((1 << kPairShift) - 1)) == 0) {
+#pragma unroll
+          for (int i = 0; i < VPL; ++i) {
+            const int v = (l16 >> kPairShift) * VPL + i;
+            s.pbuf[warp][half][v / G][v % G] = pr[i];
+            if (half == 0 && v / G == 0) s.abuf[warp][v % G] = alpha[i];
+          }
+        }
+        const bool rescale = __any_sync(kFull, moved);
+        __syncwarp();
+        // ---- PV over the half-warp's 4 tokens ----
+        if (rescale) {
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            const float a = s.abuf[warp][g];
+            const float2 aa = make_float2(a, a);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[g][c] = __fmul2_rn(acc[g][c], aa);
+          }
+        }
+#pragma unroll
+        for (int tt = 0; tt < 4; ++tt) {
+          if (t0 + tt < ntok) {
+            float2 v[4];
+            unpack8(row8(vsub, t0 + tt, chunk), v);
+            const float* pt = &s.pbuf[warp][half][tt][0];
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+              const float pg = pt[g];
+              const float2 pp = make_float2(pg, pg);
+#pragma unroll
+              for (int c = 0; c < 4; ++c) acc[g][c] = __ffma2_rn(pp, v[c], acc[g][c]);
+            }
+          }
+        }
+        __syncwarp();
+      }
+      // Release the stage; its last user refills it with stage j + kStages.
+      if (lane == 0) {
+        __threadfence_block();
+        if (atomicAdd(&s.released[stage], 1) == kConsumerWarps - 1) {
+          s.released[stage] = 0;
+          __threadfence_block();
+          fence_proxy_async_shared();
+          if (j + kStages < nstages && !*reinterpret_cast<volatile int*>(&s.abort_flag))
+            issue_stage(s, &map, p.kv_heads, kvh, n, j + kStages);
         }
       }
     }
-    __syncwarp();
   }
 
+  __syncthreads();
   if (s.abort_flag) {
-    // Drain the loads still in flight (bounded) before the CTA exits.
+    // Let the loads still in flight land (bounded) before the CTA exits.
     if (threadIdx.x == 0)
-      for (int k = consumed; k < issued; ++k)
-        mbar_wait_bounded(&s.full[k % kStages], (k / kStages) & 1, p.status);
+      for (int st = 0; st < kStages; ++st)
+        if (s.stage_issues[st] > 0)
+          mbar_wait_bounded(&s.full[st], (s.stage_issues[st] - 1) & 1, p.status);
     __syncthreads();
     return;
   }
 
-  // ---- merge the 8 warp states (log-sum-exp) ----
-  __syncthreads();  // all tiles consumed: reuse them as the merge area
-  float* accw = reinterpret_cast<float*>(s.tiles);   // [8][G][128]
-  float* mw = accw + kWarps * G * kHeadDim;           // [8][G]
-  float* lw = mw + kWarps * G;                        // [8][G]
-  float lsum = l_run + __shfl_xor_sync(kFull, l_run, G);
-  lsum += __shfl_xor_sync(kFull, lsum, 2 * G);
-  if (lane < G) {
-    mw[warp * G + lane] = m_run;
-    lw[warp * G + lane] = lsum;
-  }
+  // ---- merge the 8 warps (log-sum-exp) ----
+  float* accw = reinterpret_cast<float*>(s.tiles);    // [8][G][128]
+  float* mw = accw + kConsumerWarps * G * kHeadDim;   // [8][G]
+  float* lw = mw + kConsumerWarps * G;                // [8][G]
+  {
+    // the two half-warps hold different tokens of the same dims
 #pragma unroll
-  for (int g = 0; g < G; ++g)
-    *reinterpret_cast<float4*>(&accw[(warp * G + g) * kHeadDim + 4 * lane]) =
-        make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        acc[g][c].x += __shfl_xor_sync(kFull, acc[g][c].x, 16);
+        acc[g][c].y += __shfl_xor_sync(kFull, acc[g][c].y, 16);
+      }
+    // l of each head summed over the warp's 8 token slots
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      float ls = l_run[i] + __shfl_xor_sync(kFull, l_run[i], 4);
+      ls += __shfl_xor_sync(kFull, ls, 8);
+      ls += __shfl_xor_sync(kFull, ls, 16);
+      const int v = (l16 >> kPairShift) * VPL + i;
+      if (lane == ((v % G) / VPL) << kPairShift && v / G == 0) {
+        mw[warp * G + v % G] = m_run[i];
+        lw[warp * G + v % G] = ls;
+      }
+    }
+    if (half == 0) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float* dst = &accw[(warp * G + g) * kHeadDim + 8 * l16];
+        *reinterpret_cast<float4*>(dst) = make_float4(acc[g][0].x, acc[g][0].y, acc[g][1].x, acc[g][1].y);
+        *reinterpret_cast<float4*>(dst + 4) =
+            make_float4(acc[g][2].x, acc[g][2].y, acc[g][3].x, acc[g][3].y);
+      }
+    }
+  }
   __syncthreads();
   if (threadIdx.x < G) {
     const int g = threadIdx.x;
     float M = -INFINITY;
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, mw[w * G + g]);
+    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, mw[w * G + g]);
     float L = 0.f;
-    for (int w = 0; w < kWarps; ++w) {
+    for (int w = 0; w < kConsumerWarps; ++w) {
       const float f = (M == -INFINITY) ? 0.f : exp2f(mw[w * G + g] - M);
       s.wscale[w][g] = f;
       L += lw[w * G + g] * f;
     }
-    mw[g] = M;  // warp 0's slots are read below only through wscale/mw[g], lw[g]
-    lw[g] = L;
+    s.cta_m[g] = M;
+    s.cta_l[g] = L;
   }
   __syncthreads();
 
@@ -315,8 +428,8 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
       const int g = idx / kHeadDim, d = idx % kHeadDim;
       float o = 0.f;
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) o += accw[(w * G + g) * kHeadDim + d] * s.wscale[w][g];
-      const float L = lw[g];
+      for (int w = 0; w < kConsumerWarps; ++w) o += accw[(w * G + g) * kHeadDim + d] * s.wscale[w][g];
+      const float L = s.cta_l[g];
       const float v = L > 0.f ? o / L : 0.f;
       if (p.out_fp16) reinterpret_cast<uint16_t*>(p.out)[out_base + idx] = f2h_rn(v);
       else reinterpret_cast<float*>(p.out)[out_base + idx] = v;
@@ -329,11 +442,11 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
     const int g = idx / kHeadDim, d = idx % kHeadDim;
     float o = 0.f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) o += accw[(w * G + g) * kHeadDim + d] * s.wscale[w][g];
+    for (int w = 0; w < kConsumerWarps; ++w) o += accw[(w * G + g) * kHeadDim + d] * s.wscale[w][g];
     part[g * kPartialStride + 2 + d] = o;
     if (d == 0) {
-      part[g * kPartialStride] = mw[g];
-      part[g * kPartialStride + 1] = lw[g];
+      part[g * kPartialStride] = s.cta_m[g];
+      part[g * kPartialStride + 1] = s.cta_l[g];
     }
   }
   __threadfence();
@@ -377,12 +490,15 @@ sa_status launch_g(const AttnParams& p, const CUtensorMap& map, cudaStream_t str
 }  // namespace
 
 int attention_plan_splits(int units, int max_entries, int* split_entries) {
-  // About four waves of two CTAs per SM on 148 SMs, at least 4 entries each.
+  // About four waves of two CTAs per SM on 148 SMs; even entry counts (a
+  // stage holds two), 4..64 entries per CTA.
   const int target_ctas = 148 * 2 * 4;
   const int per_unit = std::max(1, (target_ctas + units - 1) / std::max(units, 1));
   int split = std::max(4, (max_entries + per_unit - 1) / per_unit);
-  int nsplit = std::max(1, (max_entries + split - 1) / split);
+  split = std::min(split, kMaxSplitEntries);
+  const int nsplit = std::max(1, (max_entries + split - 1) / split);
   split = std::max(1, (max_entries + nsplit - 1) / nsplit);
+  split = std::min(kMaxSplitEntries, (split + 1) & ~1);
   *split_entries = split;
   return std::max(1, (max_entries + split - 1) / split);
 }
@@ -395,6 +511,8 @@ sa_status launch_attention(const AttnParams& p, const CUtensorMap& map, cudaStre
   if (p.num_sl <= 0 || p.kv_heads <= 0) return SA_OK;
   if ((size_t)p.num_sl * p.kv_heads > 65535u)
     return fail(SA_ERR_UNSUPPORTED, "attention: more than 65535 (sequence-layer, KV head) units");
+  if (p.split_entries > kMaxSplitEntries)
+    return fail(SA_ERR_UNSUPPORTED, "attention: split larger than 64 entries");
   switch (p.group) {
     case 1: return launch_g<1>(p, map, stream);
     case 2: return launch_g<2>(p, map, stream);

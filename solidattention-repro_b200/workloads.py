@@ -1,0 +1,145 @@
+"""Synthetic decode workloads with the shapes of the path's benchmark configs.
+
+No dataset is involved: every input is seeded synthetic data generated on
+the device (torch's CUDA generator; values FP16 N(0,1), rounded to nearest
+even), the same recipe for every config:
+
+* prompt KV: FP16 N(0,1) rows for Nb sealed 32-token blocks per
+  (sequence, layer);
+* planted hot blocks: for each (layer, KV head) a seeded set of non-forced
+  blocks whose keys get +0.5 * q_hat, q_hat = the L2-normalised mean of the
+  KV head's G base decode queries (FP32 add, then RNE to FP16);
+* representatives: the online-seal build (window 32, top-4) of every block
+  from seeded N(0,1) FP16 per-token prompt queries;
+* decode step s: query = fp16(0.8 * q_base + 0.6 * z_s), z_s ~ N(0,1) (so
+  the query stays N(0,1) and correlated with the planted blocks); the new
+  token's K/V are FP16 N(0,1).
+"""
+from __future__ import annotations
+
+import dataclasses
+import math
+
+import numpy as np
+import torch
+
+from . import DecodeContext
+
+BLOCK = 32
+D = 128
+
+
+@dataclasses.dataclass(frozen=True)
+class Workload:
+    name: str
+    query_heads: int
+    kv_heads: int
+    layers: int
+    seqs: int
+    context_blocks: int   # sealed blocks at the start (context / 32)
+    budget_blocks: int
+    init_blocks: int
+    local_blocks: int
+    hot_blocks: int
+    out_fp16: bool = True
+
+    @property
+    def group(self) -> int:
+        return self.query_heads // self.kv_heads
+
+    def selected_kv_bytes(self, tail_tokens: int = 0) -> int:
+        """Algorithmic selected-KV bytes of one decode step (all layers, seqs)."""
+        per_token = 2 * self.kv_heads * D * 2
+        sel = min(self.budget_blocks, self.context_blocks)
+        return self.seqs * self.layers * (sel * BLOCK + tail_tokens) * per_token
+
+    def rep_bytes(self, blocks: int | None = None) -> int:
+        """Algorithmic representative bytes scanned by one step's scoring."""
+        nb = self.context_blocks if blocks is None else blocks
+        return self.seqs * self.layers * self.query_heads * nb * D * 4
+
+
+# The path's benchmark configs (context in 32-token blocks, budgets in blocks).
+CONFIGS = {
+    "cfg1": Workload("cfg1-qwen3-0.6b-1layer-2k-budget512", 16, 8, 1, 1, 64, 16, 1, 2, 0),
+    "cfg2": Workload("cfg2-qwen3-0.6b-28layer-16k-budget2048", 16, 8, 28, 1, 512, 64, 1, 4, 8),
+    "cfg3": Workload("cfg3-qwen3-8b-36layer-32k-budget4096", 32, 8, 36, 1, 1024, 128, 1, 4, 16),
+    "cfg5": Workload("cfg5-qwen3-8b-36layer-128k-budget8192", 32, 8, 36, 1, 4096, 256, 1, 8, 32),
+}
+
+
+def make_context(w: Workload, decode_steps: int, device: torch.device, seed: int = 0,
+                 kv_heads_slice: tuple[int, int] | None = None) -> tuple[DecodeContext, dict]:
+    """Build a DecodeContext holding workload `w`, ready for `decode_steps` steps.
+
+    kv_heads_slice=(first, count) keeps only those KV heads (and their query
+    heads) on this device: the KV-head sharding of a long single sequence.
+    Returns (ctx, info) with the base queries and hot block ids.
+    """
+    kh0, khn = kv_heads_slice or (0, w.kv_heads)
+    qh = khn * w.group
+    extra = decode_steps // BLOCK + 2
+    table_blocks = w.context_blocks + extra
+    ctx = DecodeContext(query_heads=qh, kv_heads=khn, layers=w.layers, seqs=w.seqs,
+                        pool_blocks=w.seqs * w.layers * (table_blocks + 1),
+                        table_blocks=table_blocks, budget_blocks=w.budget_blocks,
+                        init_blocks=w.init_blocks, local_blocks=w.local_blocks,
+                        out_fp16=w.out_fp16, device=device)
+    gen = torch.Generator(device=device)
+    rng = np.random.default_rng(seed)
+    nb = w.context_blocks
+    # base decode queries for the full head set, so a KV-head shard sees the
+    # same values as the unsharded sequence
+    gen.manual_seed(seed * 1000003 + 17)
+    q_base_full = torch.randn(w.seqs, w.layers, w.query_heads, D, device=device,
+                              generator=gen).half().float()
+    q_base = q_base_full[:, :, kh0 * w.group:(kh0 + khn) * w.group].contiguous()
+    hot = np.zeros((w.seqs, w.layers, w.kv_heads, w.hot_blocks), np.int64)
+    candidates = np.arange(w.init_blocks, nb - w.local_blocks)
+    for s in range(w.seqs):
+        for layer in range(w.layers):
+            phys = ctx.prefill(s, layer, nb)
+            base = int(phys[0])
+            assert (phys[:nb] == np.arange(base, base + nb)).all()
+            gen.manual_seed(seed * 1000003 + (s * w.layers + layer) * 7919 + 1)
+            kv = torch.randn(nb * BLOCK, 2, w.kv_heads, D, device=device, generator=gen).half()
+            kv = kv[:, :, kh0:kh0 + khn].contiguous()
+            for h in range(w.kv_heads):
+                ids = rng.choice(candidates, size=min(w.hot_blocks, len(candidates)), replace=False)
+                hot[s, layer, h, :len(ids)] = np.sort(ids)
+                if not (kh0 <= h < kh0 + khn) or len(ids) == 0:
+                    continue
+                grp = q_base_full[s, layer, h * w.group:(h + 1) * w.group].mean(0)
+                q_hat = grp / grp.norm()
+                rows = (torch.as_tensor(ids, device=device)[:, None] * BLOCK +
+                        torch.arange(BLOCK, device=device)[None, :]).reshape(-1)
+                k = kv[rows, 0, h - kh0].float() + 0.5 * q_hat
+                kv[rows, 0, h - kh0] = k.half()
+            ctx.pool[base:base + nb] = kv.view(nb, BLOCK, 2, khn, D)
+            del kv
+            gen.manual_seed(seed * 1000003 + (s * w.layers + layer) * 7919 + 2)
+            pq = torch.randn(w.query_heads, nb * BLOCK, D, device=device, generator=gen).half().float()
+            pq = pq[kh0 * w.group:(kh0 + khn) * w.group].contiguous()
+            ctx.build_reps(s, layer, 0, nb, pq, window=32, topk=4, per_block=True)
+            del pq
+    ctx.sync()
+    return ctx, {"q_base": q_base, "hot": hot, "qh_local": qh, "kv_heads_local": khn}
+
+
+def decode_inputs(w: Workload, info: dict, steps: int, device: torch.device, seed: int = 0,
+                  kv_heads_slice: tuple[int, int] | None = None):
+    """Per-step queries [steps][S][L][QH][D] FP32 and new K/V [steps][S][L][2][KH][D] FP16."""
+    kh0, khn = kv_heads_slice or (0, w.kv_heads)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed * 1000003 + 99)
+    q_base = info["q_base"]
+    z = torch.randn(steps, w.seqs, w.layers, w.query_heads, D, device=device, generator=gen)
+    z = z[:, :, :, kh0 * w.group:(kh0 + khn) * w.group]
+    queries = (0.8 * q_base[None] + 0.6 * z).half().float().contiguous()
+    kv = torch.randn(steps, w.seqs, w.layers, 2, w.kv_heads, D, device=device, generator=gen).half()
+    kv = kv[:, :, :, :, kh0:kh0 + khn].contiguous()
+    return queries, kv
+
+
+def scale() -> float:
+    return 1.0 / math.sqrt(D)
