@@ -95,6 +95,25 @@ SA_API sa_status sa_attention_packed(const uint16_t* kv, const float* query,
                                      void* workspace, size_t workspace_bytes,
                                      void* stream);
 
+/* The same attention for callers that cannot allocate device memory: a
+ * serving process that has already reserved all free HBM for its KV pool, a
+ * decode loop that cannot afford the device-wide synchronisation a
+ * cudaMalloc brings, or a foreign-language host with no device allocator.
+ * It allocates nothing: its split-K scratch is a 2 MiB static device array,
+ * held by every GPU that loads this library until the process exits.
+ * Problems whose workspace (sa_attention_workspace_size) exceeds 2 MiB are
+ * refused with SA_ERR_CAPACITY. The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress); make that first call before
+ * any stream capture. All calls share the one array, so calls that overlap on
+ * the GPU (other streams, other host threads) race; serialise them.
+ * This entry point has no counterpart in the reference. */
+SA_API sa_status sa_attention_packed_noalloc(const uint16_t* kv,
+                                             const float* query, size_t tokens,
+                                             size_t query_heads,
+                                             size_t kv_heads, size_t head_dim,
+                                             float scale, void* out,
+                                             int out_fp16, void* stream);
+
 /* InfLLM block scoring + init/local forcing + deterministic top-k.
  * Replaces select_shared_blocks (cpp/src/selection.cpp:96-147,
  * decl cpp/include/solidattention/selection.hpp:25-29), applied to each group
