@@ -150,6 +150,29 @@ class Port(_Lib):
         L.sao_fnv_offsets.restype = C.c_uint64
         L.sao_lifecycle_run.argtypes = [_sz] * 8 + [C.c_void_p, C.c_void_p, C.c_void_p]
 
+    def top4_first_max(self, scores):
+        s = np.ascontiguousarray(scores, np.float32)
+        out = np.zeros(4, np.int64)
+        self.lib.sao_top4_first_max.argtypes = [_f32p, _sz, _i64p]
+        self.lib.sao_top4_first_max(s, s.size, out)
+        return out
+
+    def received_mass(self, prompt_q, kv, tokens, qh, kh, d, block_tokens, window, topk):
+        """Per-(head, token) received mass of the representative build."""
+        blocks = tokens // block_tokens
+        received = np.zeros(qh * tokens, np.float32)
+        values = np.zeros(max(qh * blocks * d, 1), np.float32)
+        offsets = np.zeros(max(qh * blocks * topk, 1), np.int64)
+        pq = np.ascontiguousarray(prompt_q, np.float32)
+        kvc = np.ascontiguousarray(kv, np.uint16)
+        fn = self.lib.sao_build_representatives
+        fn.argtypes = [C.c_void_p, C.c_void_p] + [_sz] * 7 + [C.c_void_p] * 3
+        rc = fn(pq.ctypes.data, kvc.ctypes.data, tokens, qh, kh, d, block_tokens, window, topk,
+                values.ctypes.data, offsets.ctypes.data, received.ctypes.data)
+        if rc != 0:
+            raise ValueError("invalid local-causal representative dimensions")
+        return received.reshape(qh, tokens)
+
     def half_to_float(self, h):
         h = np.ascontiguousarray(h, np.uint16)
         out = np.empty(h.size, np.float32)

@@ -510,3 +510,20 @@ int sao_sparse_step(const uint16_t* pool, const int32_t* table,
   }
   return failed ? -1 : 0;
 }
+
+/* kv_lifecycle_main.cpp:93-103: the four highest-scoring in-block offsets,
+ * each pass taking the first strict maximum among offsets not yet taken. */
+void sao_top4_first_max(const float* scores, size_t block_tokens, int64_t* out) {
+  size_t top[4] = {0, 0, 0, 0};
+  for (size_t rank = 0; rank < 4; ++rank) {
+    size_t best = block_tokens;
+    for (size_t t = 0; t < block_tokens; ++t) {
+      int taken = 0;
+      for (size_t r = 0; r < rank; ++r) taken |= top[r] == t;
+      if (taken) continue;
+      if (best == block_tokens || scores[t] > scores[best]) best = t;
+    }
+    top[rank] = best;
+    out[rank] = (int64_t)best;
+  }
+}

@@ -132,6 +132,10 @@ int sao_sparse_step(const uint16_t* pool, const int32_t* table,
                     size_t init, size_t local, float scale, int threads,
                     int64_t* ids_out, float* out);
 
+/* The lifecycle's representative audit (kv_lifecycle_main.cpp:93-103): four
+ * in-block offsets by descending score, first maximum wins. */
+void sao_top4_first_max(const float* scores, size_t block_tokens, int64_t* out);
+
 /* FNV-1a over 64-bit words, as the C2.1 driver hashes representative offsets
  * (cpp/src/selection_main.cpp:167-171). */
 uint64_t sao_fnv_offsets(const int64_t* values, size_t n);

@@ -1,0 +1,225 @@
+"""The CPU oracle against the reference's own outputs and published answers.
+
+* golden_ref.npz: outputs of the reference's C++ (compiled from its sources)
+  on seeded cases -- the C restatement must match them bit for bit;
+* the reference's published known answers (C2.1 selection, P1.3b.0 lifecycle);
+* python_twins.json: the reference's Python twins on their own test inputs;
+* when oracle/_ref is built, the restatement against the reference directly.
+"""
+from __future__ import annotations
+
+import json
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+sys.path.insert(0, str(GOLDEN))
+import cases  # noqa: E402
+
+from conftest import cosine  # noqa: E402
+
+
+@pytest.fixture(scope="module")
+def golden():
+    return np.load(GOLDEN / "golden_ref.npz")
+
+
+@pytest.fixture(scope="module")
+def twins():
+    return json.loads((GOLDEN / "python_twins.json").read_text())
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+# --------------------------------------------- golden vectors of the reference
+
+@pytest.mark.parametrize("i", range(len(cases.ATTENTION)))
+def test_attention_matches_reference_outputs(port, golden, i):
+    kv, q, tokens, qh, kh = cases.attention_case(i)
+    assert cases.digest(kv, q) == str(golden[f"attn{i}_sha"])
+    got = port.attention(kv, q, tokens, qh, kh, 128, cases.SCALE).ravel()
+    assert np.array_equal(bits(got), bits(golden[f"attn{i}_out"]))
+
+
+@pytest.mark.parametrize("i", range(len(cases.SELECTION)))
+def test_selection_matches_reference_outputs(port, golden, i):
+    q, reps, qh, group, blocks, budget, init, local = cases.selection_case(i)
+    assert cases.digest(q, reps) == str(golden[f"sel{i}_sha"])
+    ids, scores = port.select_grouped(q, reps, qh, group, blocks, 128, budget, init, local)
+    assert np.array_equal(ids, golden[f"sel{i}_ids"])
+    assert np.array_equal(bits(scores), bits(golden[f"sel{i}_scores"]))
+
+
+@pytest.mark.parametrize("i", range(len(cases.REPRESENTATIVES)))
+def test_representatives_match_reference_outputs(port, golden, i):
+    kv, pq, tokens, qh, kh, window, topk = cases.representatives_case(i)
+    assert cases.digest(kv, pq) == str(golden[f"rep{i}_sha"])
+    vals, offs = port.build_representatives(pq, kv, tokens, qh, kh, 128, 32, window, topk)
+    assert np.array_equal(bits(vals), bits(golden[f"rep{i}_values"]))
+    assert np.array_equal(offs, golden[f"rep{i}_offsets"])
+
+
+# ----------------------------------------------- published known answers
+
+def test_c21_known_answer(port):
+    """docs/cpp-versions/C2.1-infllm-selection-uring.md:40,67 and
+    artifacts/runs/*C2.1*-metrics.json: offset hash 7873450381430813043,
+    blocks [0, 8, 13, 15], selected-vs-dense cosine 0.987693."""
+    kv, pq, q = port.c21_fixture()
+    vals, offs = port.build_representatives(pq, kv, 512, 16, 8, 128, 32, 32, 4)
+    assert port.fnv_offsets(offs) == 7873450381430813043
+    ids, _ = port.select_shared_blocks(q, vals, 16, 16, 128, 4, 1, 1)
+    assert ids.tolist() == [0, 8, 13, 15]
+    packed = port.gather_packed(kv, ids, 32, None, 0, 2048)
+    sparse = port.attention(packed, q, 128, 16, 8, 128, cases.SCALE)
+    dense = port.attention(kv, q, 512, 16, 8, 128, cases.SCALE)
+    assert round(cosine(sparse, dense), 6) == 0.987693
+
+
+def test_p13b0_lifecycle_known_answer(port):
+    """docs/native-pipeline/P1.3b0-native-kv-lifecycle.md:22-28: 28 layers x
+    512 tokens -> 448 sealed blocks, 7,168 representative audits, tail 32,
+    generation 16, store of 121,110,528 bytes."""
+    r = port.lifecycle_run(28, 16, 8, 128, 32, 32, 512, 16)
+    assert r["sealed_total"] == 448
+    assert r["representative_audits"] == 7168
+    assert r["tail_tokens_layer0"] == 32
+    assert r["generation_layer0"] == 16
+    assert 28 * r["capacity_blocks"] * 32 * 2 * 8 * 128 * 2 == 121_110_528
+
+
+def test_seal_boundary(port):
+    """63 resident tokens do not seal; the 64th seals one block, leaving 32
+    (tests/test_kv_lifecycle.py:13-37 and the P1.3b.0 boundary test)."""
+    r = port.lifecycle_run(1, 4, 2, 2, 32, 32, 31, 0)
+    assert r["sealed_total"] == 0 and r["tail_tokens_layer0"] == 63
+    r = port.lifecycle_run(1, 4, 2, 2, 32, 32, 32, 0)
+    assert r["sealed_total"] == 1 and r["tail_tokens_layer0"] == 32
+
+
+def test_c1_fixture_attention_port_equals_reference(port, ref):
+    """C1 (cpp/src/attention_main.cpp:118-160): the restated fixture through the
+    restated attention equals the reference's attention bit for bit."""
+    kv, q = port.c1_fixture()
+    out = port.attention(kv, q, 128, 16, 8, 128, np.float32(0.08838834764831845))
+    want = ref.attention(kv, q, 128, 16, 8, 128, np.float32(0.08838834764831845))
+    assert np.array_equal(bits(out), bits(want))
+
+
+# ---------------------------------------------------------- Python twins
+
+def test_window1_masses_match_python_twin(port, twins):
+    """tests/test_selection.py:6-12: with window 1 every key receives mass 1."""
+    q = np.array([[10.0, 0.0], [0.0, 10.0]], np.float32)          # [T=2][D=2], one head
+    kv = np.zeros((2, 2, 1, 2), np.uint16)
+    kv[:, 0, 0] = q.astype(np.float16).view(np.uint16)
+    kv[:, 1, 0] = kv[:, 0, 0]
+    mass = port.received_mass(q.reshape(1, 2, 2), kv, 2, 1, 1, 2, 1, 1, 1)
+    assert mass.tolist() == twins["window1_scores"]
+
+
+def test_received_masses_match_python_twin(port, twins):
+    c = twins["masses_case"]
+    qh, kh, tokens, d = 4, 2, 64, 16
+    q = np.array(c["query"], np.uint16).view(np.float16).astype(np.float32).reshape(qh, tokens, d)
+    key = np.array(c["key"], np.uint16).reshape(kh, tokens, d)
+    kv = np.zeros((tokens, 2, kh, d), np.uint16)
+    kv[:, 0] = key.transpose(1, 0, 2)
+    kv[:, 1] = key.transpose(1, 0, 2)
+    mass = port.received_mass(q, kv, tokens, qh, kh, d, 32, c["window"], 4)
+    want = np.array(c["scores"], np.float32).reshape(qh, tokens)
+    assert np.abs(mass - want).max() <= 2e-5  # torch's batched softmax rounds differently
+
+
+def test_gqa_selection_matches_python_twin(port, twins):
+    """tests/test_selection.py:15-23 (the twin accepts [0] or [1]; the C++
+    selector, and so this build, returns [0])."""
+    c = twins["gqa_select"]
+    q = np.array(c["query"], np.float32)
+    reps = np.array(c["reps"], np.float32)
+    ids, _ = port.select_shared_blocks(q, reps, 2, 2, 2, 1, 0, 0)
+    assert ids.tolist() == c["chosen"] == [0]
+
+
+def test_lifecycle_twin_planted_indices(port, twins):
+    """tests/test_kv_lifecycle.py:22-37: planted scores at 7, 9, 11, 13 give
+    those four representative indices; the C++ audit rule agrees."""
+    t = twins["tail64"]
+    assert t["sealed"] == 1 and t["length"] == 32
+    assert port.top4_first_max(np.array(t["planted_scores"], np.float32)).tolist() == t["indices"][0]
+    assert twins["tail63"] == {"sealed": 0, "length": 63}
+
+
+# ---------------------------------------------------------------- numerics
+
+def test_half_to_float_is_exact_for_every_pattern(port):
+    h = np.arange(65536, dtype=np.uint16)
+    got = port.half_to_float(h)
+    want = h.view(np.float16).astype(np.float32)
+    nan = np.isnan(want)
+    assert np.array_equal(got[~nan].view(np.uint32), want[~nan].view(np.uint32))
+    assert np.isnan(got[nan]).all()
+
+
+def test_rne_conversion_matches_numpy(port):
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.standard_normal(200_000, dtype=np.float32) * 3,
+                        np.array([0.0, -0.0, 1.9999, 0.49999, 65504, 65519, 65520, 1e9, -1e9,
+                                  6e-8, 5.96e-8, 2.98e-8, 2 ** -25, 2 ** -24 * 1.5, np.inf, -np.inf],
+                                 np.float32)])
+    with np.errstate(over="ignore"):
+        want = x.astype(np.float16).view(np.uint16)
+    assert np.array_equal(port.float_to_half_rne(x), want)
+
+
+def test_reference_float_to_half_drops_the_carry(port, ref):
+    """The reference's conversion (attention_reference.cpp:11-28) is not RNE:
+    1.9999f becomes 1.0 (the rounded mantissa carry is lost)."""
+    for v in (1.9999, 0.49999, 0.1, -3.3):
+        assert port.lib.sao_ref_float_to_half(v) == ref.float_to_half(v)
+    assert np.uint16(port.lib.sao_ref_float_to_half(1.9999)).view(np.float16) == np.float16(1.0)
+
+
+# ------------------------------------------------- restatement vs reference
+
+@pytest.mark.parametrize("seed", range(3))
+def test_port_equals_reference_on_random_cases(port, ref, seed):
+    rng = np.random.default_rng(1000 + seed)
+    tokens, qh, kh = int(rng.integers(1, 300)), 8, 2
+    kv = cases.fp16(rng, tokens * 2 * kh * 128)
+    q = rng.standard_normal(qh * 128, dtype=np.float32)
+    a = port.attention(kv, q, tokens, qh, kh, 128, cases.SCALE)
+    b = ref.attention(kv, q, tokens, qh, kh, 128, cases.SCALE)
+    assert np.array_equal(bits(a), bits(b))
+    blocks = int(rng.integers(8, 200))
+    reps = rng.standard_normal((qh, blocks, 128), dtype=np.float32)
+    qq = rng.standard_normal((qh, 128), dtype=np.float32)
+    i1, s1 = port.select_grouped(qq, reps, qh, 4, blocks, 128, 8, 1, 2)
+    i2, s2 = ref.select_grouped(qq, reps, qh, 4, blocks, 128, 8, 1, 2)
+    assert np.array_equal(i1, i2) and np.array_equal(bits(s1), bits(s2))
+    t = 32 * int(rng.integers(1, 4))
+    pq = cases.fp16(rng, 4 * t * 128).view(np.float16).astype(np.float32)
+    kv2 = cases.fp16(rng, t * 2 * 2 * 128)
+    v1, o1 = port.build_representatives(pq, kv2, t, 4, 2, 128, 32, 17, 4)
+    v2, o2 = ref.build_representatives(pq, kv2, t, 4, 2, 128, 32, 17, 4)
+    assert np.array_equal(bits(v1), bits(v2)) and np.array_equal(o1, o2)
+
+
+def test_cpu_step_port_equals_reference(port, ref):
+    """The CPU decode step used as the baseline: restatement == reference."""
+    rng = np.random.default_rng(7)
+    layers, qh, kh, nb = 2, 8, 2, 20
+    tv = 2 * kh * 128
+    pool = cases.fp16(rng, layers * (nb + 1) * 32 * tv)
+    table = np.stack([np.arange(nb, dtype=np.int32) + i * (nb + 1) for i in range(layers)])
+    tails = np.array([i * (nb + 1) + nb for i in range(layers)], np.int32)
+    reps = rng.standard_normal((layers, qh, nb, 128), dtype=np.float32)
+    q = rng.standard_normal((layers, qh, 128), dtype=np.float32)
+    a = port.sparse_step(pool, table, reps, q, tails, 9, qh, kh, 128, 32, nb, 6, 1, 2, cases.SCALE, 2)
+    b = ref.sparse_step(pool, table, reps, q, tails, 9, qh, kh, 128, 32, nb, 6, 1, 2, cases.SCALE, 2)
+    assert np.array_equal(a[0], b[0]) and np.array_equal(bits(a[1]), bits(b[1]))
