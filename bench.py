@@ -143,7 +143,7 @@ def host_sample_from_ctx(ctx, layers):
     pools, table_rows, tail_rows, reps = [], [], [], []
     for i, l in enumerate(layers):
         phys = np.concatenate([tables[l, :nb], tails[l:l + 1]]).astype(np.int64)
-        pools.append(ctx.pool[torch.as_tensor(phys, device=ctx.device)].cpu().numpy().view(np.uint16))
+        pools.append(ctx.read_blocks(phys).cpu().numpy().view(np.uint16))
         table_rows.append(np.arange(nb, dtype=np.int32) + i * (nb + 1))
         tail_rows.append(i * (nb + 1) + nb)
         reps.append(ctx.reps[l, :, :, :nb].permute(0, 2, 1).contiguous().cpu().numpy())

@@ -173,8 +173,9 @@ typedef struct {
   double d2h_ms;
 } sa_timings;
 
-#define SA_ATTN_COPY_OUTPUT 0x1 /* D2H the FP32 output into out_host          */
-#define SA_ATTN_CONSUME 0x2     /* run the checksum consumer; out_host[0] gets
+#define SA_ATTN_COPY_OUTPUT 0x1 /* D2H into out_host: the FP32 output, or with
+                                   SA_ATTN_CONSUME the checksum (1 float)     */
+#define SA_ATTN_CONSUME 0x2     /* run the checksum consumer on the device:
                                    sum(out[i] * (1 + (i % 17) * 1e-3))        */
 
 SA_API sa_status sa_backend_create(int device, sa_backend** out);
@@ -189,6 +190,26 @@ SA_API sa_status sa_backend_attention(sa_backend* backend,
                                       size_t query_heads, size_t kv_heads,
                                       size_t head_dim, float scale, int flags,
                                       float* out_host, sa_timings* timings);
+/* Host-buffer selection with the reference's signature and semantics
+ * (select_shared_blocks, cpp/src/selection.cpp:96-147): reps in the reference
+ * layout [query_heads][blocks][head_dim]; one shared selection over all query
+ * heads. ids_out_host receives budget_blocks ids ascending; scores_out_host
+ * (nullable) the blocks' mean_head_scores. Synchronous. */
+SA_API sa_status sa_backend_select(sa_backend* backend, const float* query_host,
+                                   const float* reps_host, size_t query_heads,
+                                   size_t blocks, size_t head_dim,
+                                   size_t budget_blocks, size_t init_blocks,
+                                   size_t local_blocks, int64_t* ids_out_host,
+                                   float* scores_out_host);
+/* Host-buffer representative build with the reference's signature and
+ * semantics (build_local_causal_representatives, cpp/src/selection.cpp:12-94):
+ * values_out_host [query_heads][tokens/block_tokens][head_dim],
+ * offsets_out_host [query_heads][tokens/block_tokens][topk]. Synchronous. */
+SA_API sa_status sa_backend_build_representatives(
+    sa_backend* backend, const float* prompt_queries_host,
+    const uint16_t* kv_host, size_t tokens, size_t query_heads,
+    size_t kv_heads, size_t head_dim, size_t block_tokens, size_t local_window,
+    size_t topk, float* values_out_host, int64_t* offsets_out_host);
 /* C0 transport smoke: out = in ^ mask over `bytes`, checksum of the bytes
  * (cpp/src/cuda_backend.cpp:242-280). */
 SA_API sa_status sa_backend_execute(sa_backend* backend, void* pinned_input,
@@ -231,7 +252,8 @@ typedef struct {
 
 /* Device pointers owned by a context, for callers that fill or inspect it. */
 typedef struct {
-  uint16_t* pool;         /* [pool_blocks][32][2][KH][D] */
+  uint16_t* pool;         /* [pool_blocks][KH][2 (K,V)][32][D]: head-major
+                             blocks, one 16 KB K+V run per (block, head) */
   float* reps;            /* [seqs*layers][QH][D][table_blocks] */
   int32_t* table;         /* [seqs*layers][table_blocks] logical -> physical */
   int32_t* num_sealed;    /* [seqs*layers] */

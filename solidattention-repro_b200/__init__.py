@@ -183,7 +183,8 @@ class Backend:
         kv = np.ascontiguousarray(kv, np.uint16)
         query = np.ascontiguousarray(query, np.float32)
         out = np.zeros(1 if consume else query_heads * head_dim, np.float32)
-        flags = (SA_ATTN_COPY_OUTPUT if copy_output else 0) | (SA_ATTN_CONSUME if consume else 0)
+        flags = (SA_ATTN_COPY_OUTPUT if copy_output or consume else 0) | \
+            (SA_ATTN_CONSUME if consume else 0)
         t = Timings()
         check(self._lib.sa_backend_attention(self._h, kv.ctypes.data, query.ctypes.data, tokens,
                                              query_heads, kv_heads, head_dim, C.c_float(scale),
@@ -221,7 +222,10 @@ class DecodeContext:
     created (so torch ops and CUDA events order with them). Tensor attributes
     are zero-copy views of the context's device buffers:
 
-    ``pool`` [pool_blocks, 32, 2, KH, 128] FP16; ``reps`` [S*L, QH, 128, cap];
+    ``pool`` [pool_blocks, KH, 2, 32, 128] FP16 (head-major blocks: K rows then
+    V rows of one KV head are one contiguous 16 KB run; ``write_blocks`` /
+    ``read_blocks`` convert from / to the reference's token-major rows
+    [blocks, 32, 2, KH, 128]); ``reps`` [S*L, QH, 128, cap];
     ``table`` [S*L, table_blocks]; ``num_sealed``/``tail_block``/``tail_len``/
     ``generation`` [S*L]; ``query_ring`` [S*L, QH, 32, 128];
     ``selected`` [S*L, groups, budget]; ``selected_count`` [S*L, groups];
@@ -265,7 +269,7 @@ class DecodeContext:
         self.cap = (table_blocks + 3) & ~3
         self.out_fp16 = bool(out_fp16)
         d, n = self.device, self.num_sl
-        self.pool = _view(p.pool, (pool_blocks, BLOCK_TOKENS, 2, kv_heads, head_dim), torch.float16, d)
+        self.pool = _view(p.pool, (pool_blocks, kv_heads, 2, BLOCK_TOKENS, head_dim), torch.float16, d)
         self.reps = _view(p.reps, (n, query_heads, head_dim, self.cap), torch.float32, d)
         self.table = _view(p.table, (n, table_blocks), torch.int32, d)
         self.num_sealed = _view(p.num_sealed, (n,), torch.int32, d)
@@ -282,6 +286,17 @@ class DecodeContext:
         self.status = _view(p.status, (1,), torch.int32, d)
 
     # ---- setup
+    def write_blocks(self, phys, kv_token_major: torch.Tensor) -> None:
+        """Store token-major blocks [n, 32, 2, KH, 128] (the reference's row
+        layout) into pool blocks `phys` (head-major)."""
+        idx = torch.as_tensor(np.asarray(phys, np.int64), device=self.device)
+        self.pool[idx] = kv_token_major.to(self.device).permute(0, 3, 2, 1, 4).to(torch.float16)
+
+    def read_blocks(self, phys) -> torch.Tensor:
+        """Pool blocks `phys` as token-major rows [n, 32, 2, KH, 128]."""
+        idx = torch.as_tensor(np.asarray(phys, np.int64), device=self.device)
+        return self.pool[idx].permute(0, 3, 2, 1, 4).contiguous()
+
     def reset(self) -> None:
         check(self._lib.sa_ctx_reset(self._h), "sa_ctx_reset")
 

@@ -84,6 +84,9 @@ PROTOTYPES = {
     "sa_backend_host_free": (C.c_int, [_vp, _vp]),
     "sa_backend_attention": (C.c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _sz, C.c_float, C.c_int,
                                        _vp, C.POINTER(Timings)]),
+    "sa_backend_select": (C.c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _sz, _sz, _sz, _vp, _vp]),
+    "sa_backend_build_representatives": (C.c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _sz, _sz, _sz,
+                                                   _sz, _vp, _vp]),
     "sa_backend_execute": (C.c_int, [_vp, _vp, _sz, C.c_uint8, C.POINTER(Timings),
                                      C.POINTER(C.c_uint64)]),
     "sa_ctx_create": (C.c_int, [C.POINTER(CtxConfig), C.POINTER(_vp)]),

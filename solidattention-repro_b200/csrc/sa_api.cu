@@ -88,11 +88,11 @@ sa_status make_row_tensor_map(CUtensorMap* map, const void* base, uint64_t row_e
   if (rows == 0 || rows > 0xffffffffull) return fail(SA_ERR_UNSUPPORTED, "KV rows out of TMA range");
   const cuuint64_t dims[2] = {row_elems, rows};
   const cuuint64_t strides[1] = {row_elems * sizeof(uint16_t)};
-  const cuuint32_t box[2] = {64, (cuuint32_t)kBlockTokens};
+  const cuuint32_t box[2] = {(cuuint32_t)kHeadDim, (cuuint32_t)kBlockTokens};
   const cuuint32_t elem_strides[2] = {1, 1};
   const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims,
                             strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(SA_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
@@ -120,6 +120,8 @@ struct sa_backend {
   size_t ws_cap = 0;
   uint8_t* d_io = nullptr;
   size_t io_cap = 0;
+  void* d_buf[6] = {};     // selection / representative staging
+  size_t buf_cap[6] = {};
 };
 
 struct sa_ctx {
@@ -196,6 +198,8 @@ SA_API sa_status sa_attention_packed(const uint16_t* kv, const float* query, siz
   const int entries = (int)((tokens + kBlockTokens - 1) / kBlockTokens);
   const int units = (int)kv_heads;
   AttnParams p{};
+  p.pool = nullptr;
+  p.head_major = 0;
   p.kv_heads = (int)kv_heads;
   p.group = (int)(query_heads / kv_heads);
   p.num_sl = 1;
@@ -306,6 +310,7 @@ SA_API sa_status sa_build_representatives(const float* prompt_queries, const uin
   if (!values_out) return fail(SA_ERR_INVALID_ARG, "representatives: null values_out");
   RepParams p{};
   p.kv = kv;
+  p.head_major = 0;
   p.row_stride = (int64_t)(2 * kv_heads * head_dim);
   p.table = nullptr;
   p.table_offset = 0;
@@ -365,6 +370,7 @@ SA_API sa_status sa_backend_destroy(sa_backend* b) {
   cudaFree(b->d_checksum);
   cudaFree(b->d_ws);
   cudaFree(b->d_io);
+  for (void* p : b->d_buf) cudaFree(p);
   for (auto& e : b->ev)
     if (e) cudaEventDestroy(e);
   if (b->stream) cudaStreamDestroy(b->stream);
@@ -409,7 +415,7 @@ SA_API sa_status sa_backend_attention(sa_backend* b, const uint16_t* kv_host,
   if (kv_heads == 0 || query_heads % kv_heads != 0 || tokens == 0)
     return fail(SA_ERR_INVALID_ARG, "invalid GQA attention dimensions");
   if (head_dim != (size_t)kHeadDim) return fail(SA_ERR_UNSUPPORTED, "attention: head_dim must be 128");
-  if ((flags & (SA_ATTN_COPY_OUTPUT | SA_ATTN_CONSUME)) && !out_host)
+  if ((flags & SA_ATTN_COPY_OUTPUT) && !out_host)
     return fail(SA_ERR_INVALID_ARG, "backend attention: null out_host");
   DeviceGuard guard(b->device);
   const size_t kv_bytes = tokens * 2 * kv_heads * head_dim * sizeof(uint16_t);
@@ -434,7 +440,7 @@ SA_API sa_status sa_backend_attention(sa_backend* b, const uint16_t* kv_host,
       return st;
   }
   SA_CUDA_TRY(cudaEventRecord(b->ev[3], b->stream));
-  if (flags & (SA_ATTN_COPY_OUTPUT | SA_ATTN_CONSUME)) {
+  if (flags & SA_ATTN_COPY_OUTPUT) {
     SA_CUDA_TRY(cudaMemcpyAsync(out_host, consume ? b->d_checksum : b->d_out,
                                 consume ? sizeof(float) : q_bytes, cudaMemcpyDeviceToHost,
                                 b->stream));
@@ -449,6 +455,88 @@ SA_API sa_status sa_backend_attention(sa_backend* b, const uint16_t* kv_host,
     timings->consumer_ms = ms[2];
     timings->d2h_ms = ms[3];
   }
+  return SA_OK;
+}
+
+SA_API sa_status sa_backend_select(sa_backend* b, const float* query_host, const float* reps_host,
+                                   size_t query_heads, size_t blocks, size_t head_dim,
+                                   size_t budget_blocks, size_t init_blocks, size_t local_blocks,
+                                   int64_t* ids_out_host, float* scores_out_host) {
+  if (!b) return fail(SA_ERR_INVALID_ARG, "backend select: null backend");
+  // The reference's own validation (cpp/src/selection.cpp:99-105).
+  if (!query_host || !reps_host || query_heads == 0 || blocks == 0 || head_dim == 0 ||
+      budget_blocks == 0 || budget_blocks > blocks || init_blocks + local_blocks > budget_blocks)
+    return fail(SA_ERR_INVALID_ARG, "invalid representative selection dimensions");
+  if (!ids_out_host) return fail(SA_ERR_INVALID_ARG, "backend select: null ids_out_host");
+  DeviceGuard guard(b->device);
+  const size_t q_bytes = query_heads * head_dim * sizeof(float);
+  const size_t r_bytes = query_heads * blocks * head_dim * sizeof(float);
+  const size_t ws_bytes = sa_select_workspace_size(query_heads, query_heads, blocks);
+  const size_t sizes[5] = {q_bytes, r_bytes, budget_blocks * 4, blocks * 4, ws_bytes};
+  for (int i = 0; i < 5; ++i) {
+    const sa_status st = grow(&b->d_buf[i], &b->buf_cap[i], sizes[i]);
+    if (st != SA_OK) return st;
+  }
+  SA_CUDA_TRY(cudaMemcpyAsync(b->d_buf[0], query_host, q_bytes, cudaMemcpyHostToDevice, b->stream));
+  SA_CUDA_TRY(cudaMemcpyAsync(b->d_buf[1], reps_host, r_bytes, cudaMemcpyHostToDevice, b->stream));
+  const sa_status st = sa_select_blocks(
+      static_cast<const float*>(b->d_buf[0]), static_cast<const float*>(b->d_buf[1]),
+      (int64_t)(blocks * head_dim), (int64_t)head_dim, 1, query_heads, query_heads, blocks, head_dim,
+      budget_blocks, init_blocks, local_blocks, static_cast<int32_t*>(b->d_buf[2]),
+      static_cast<float*>(b->d_buf[3]), b->d_buf[4], b->buf_cap[4], b->stream);
+  if (st != SA_OK) return st;
+  std::vector<int32_t> ids(budget_blocks);
+  SA_CUDA_TRY(cudaMemcpyAsync(ids.data(), b->d_buf[2], budget_blocks * 4, cudaMemcpyDeviceToHost,
+                              b->stream));
+  if (scores_out_host)
+    SA_CUDA_TRY(cudaMemcpyAsync(scores_out_host, b->d_buf[3], blocks * 4, cudaMemcpyDeviceToHost,
+                                b->stream));
+  SA_CUDA_TRY(cudaStreamSynchronize(b->stream));
+  for (size_t i = 0; i < budget_blocks; ++i) ids_out_host[i] = ids[i];
+  return SA_OK;
+}
+
+SA_API sa_status sa_backend_build_representatives(sa_backend* b, const float* prompt_queries_host,
+                                                  const uint16_t* kv_host, size_t tokens,
+                                                  size_t query_heads, size_t kv_heads,
+                                                  size_t head_dim, size_t block_tokens,
+                                                  size_t local_window, size_t topk,
+                                                  float* values_out_host,
+                                                  int64_t* offsets_out_host) {
+  if (!b) return fail(SA_ERR_INVALID_ARG, "backend representatives: null backend");
+  // The reference's own validation (cpp/src/selection.cpp:17-22).
+  if (!prompt_queries_host || !kv_host || tokens == 0 || kv_heads == 0 ||
+      query_heads % kv_heads != 0 || block_tokens == 0 || tokens % block_tokens != 0 ||
+      local_window == 0 || topk == 0 || topk > block_tokens)
+    return fail(SA_ERR_INVALID_ARG, "invalid local-causal representative dimensions");
+  if (!values_out_host) return fail(SA_ERR_INVALID_ARG, "backend representatives: null values_out");
+  DeviceGuard guard(b->device);
+  const size_t blocks = tokens / block_tokens;
+  const size_t q_bytes = query_heads * tokens * head_dim * sizeof(float);
+  const size_t kv_bytes = tokens * 2 * kv_heads * head_dim * sizeof(uint16_t);
+  const size_t v_bytes = query_heads * blocks * head_dim * sizeof(float);
+  const size_t o_bytes = query_heads * blocks * topk * sizeof(int32_t);
+  const size_t sizes[4] = {q_bytes, kv_bytes, v_bytes, o_bytes};
+  for (int i = 0; i < 4; ++i) {
+    const sa_status st = grow(&b->d_buf[i], &b->buf_cap[i], sizes[i]);
+    if (st != SA_OK) return st;
+  }
+  SA_CUDA_TRY(cudaMemcpyAsync(b->d_buf[0], prompt_queries_host, q_bytes, cudaMemcpyHostToDevice,
+                              b->stream));
+  SA_CUDA_TRY(cudaMemcpyAsync(b->d_buf[1], kv_host, kv_bytes, cudaMemcpyHostToDevice, b->stream));
+  const sa_status st = sa_build_representatives(
+      static_cast<const float*>(b->d_buf[0]), static_cast<const uint16_t*>(b->d_buf[1]), tokens,
+      query_heads, kv_heads, head_dim, block_tokens, local_window, topk,
+      static_cast<float*>(b->d_buf[2]), static_cast<int32_t*>(b->d_buf[3]), b->stream);
+  if (st != SA_OK) return st;
+  std::vector<int32_t> offsets(query_heads * blocks * topk);
+  SA_CUDA_TRY(cudaMemcpyAsync(values_out_host, b->d_buf[2], v_bytes, cudaMemcpyDeviceToHost,
+                              b->stream));
+  SA_CUDA_TRY(cudaMemcpyAsync(offsets.data(), b->d_buf[3], o_bytes, cudaMemcpyDeviceToHost,
+                              b->stream));
+  SA_CUDA_TRY(cudaStreamSynchronize(b->stream));
+  if (offsets_out_host)
+    for (size_t i = 0; i < offsets.size(); ++i) offsets_out_host[i] = offsets[i];
   return SA_OK;
 }
 
@@ -558,6 +646,8 @@ sa_status ctx_select(sa_ctx* c, const float* query) {
 
 sa_status ctx_attend(sa_ctx* c, const float* query, void* out) {
   AttnParams p{};
+  p.pool = c->dev.pool;
+  p.head_major = 1;
   p.kv_heads = c->cfg.kv_heads;
   p.group = c->group;
   p.num_sl = c->num_sl;
@@ -651,9 +741,8 @@ SA_API sa_status sa_ctx_create(const sa_ctx_config* config, sa_ctx** out) {
     st = cuda_status(cudaHostAlloc(reinterpret_cast<void**>(&c->h_status), sizeof(uint32_t),
                                    cudaHostAllocDefault),
                      "cudaHostAlloc status");
-  if (st == SA_OK)
-    st = make_row_tensor_map(&c->pool_map, d.pool, (uint64_t)row_elems,
-                             (uint64_t)g.pool_blocks * kBlockTokens);
+  // The pool is head-major and read with bulk copies: no tensor map.
+  std::memset(&c->pool_map, 0, sizeof(c->pool_map));
   if (st == SA_OK) {
     SA_CUDA_TRY(cudaMemset(d.pool, 0, (size_t)g.pool_blocks * kBlockTokens * row_elems * 2));
     SA_CUDA_TRY(cudaMemset(d.reps, 0, nsl * g.query_heads * kHeadDim * (size_t)c->table_pad * 4));
@@ -788,6 +877,7 @@ SA_API sa_status sa_ctx_build_reps(sa_ctx* c, int32_t seq, int32_t layer, int32_
   const int sl = seq * g.layers + layer;
   RepParams p{};
   p.kv = c->dev.pool;
+  p.head_major = 1;
   p.row_stride = c->dev.row_elems;
   p.table = c->dev.table;
   p.table_offset = sl * g.table_blocks + first;

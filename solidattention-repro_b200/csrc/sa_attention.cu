@@ -12,16 +12,18 @@
 // (physical block, token count) pairs are resolved once, in parallel, into
 // shared memory.
 //
-// Pipeline: a stage holds two entries (2 x 16 KB: K lo/hi and V lo/hi of the
-// unit's KV head, 32 rows x 128 B per sub-tile, 128 B TMA swizzle) in a ring
-// of three stages. A stage's TMA loads complete a "full" mbarrier (bounded
+// Pipeline: a stage holds two entries (2 x 16 KB: the K rows then the V rows
+// of the unit's KV head, 32 x 256 B each) in a ring of three stages. Entries
+// of the decode context's head-major pool arrive as one contiguous 16 KB
+// bulk copy; entries of a caller's token-major buffer as two 8 KB TMA tiles
+// (32 rows x 256 B) -- the shared-memory layout is the same. A stage's TMA loads complete a "full" mbarrier (bounded
 // waits); the last of the eight warps to release a stage (a shared-memory
 // arrival counter) issues the loads that refill it, so no warp ever blocks
 // on a producer.
 //
 // Consumer warp w, per stage: half-warp h takes entry h of the stage and its
-// tokens [4w, 4w+4); lane l covers head dims [8(l%16), 8(l%16)+8). Each row is
-// read as one conflict-free 128-bit swizzled shared load. QK uses packed FP32
+// tokens [4w, 4w+4); lane l covers head dims [8(l%16), 8(l%16)+8). A
+// quarter-warp reads 128 contiguous bytes of one row: conflict-free. QK uses packed FP32
 // FMA (__ffma2_rn) with the softmax scale folded into q, then a 16-lane
 // transpose-reduce leaves one (token, head) logit per lane. The warp keeps an
 // FP32 online softmax per head (exp2 domain, running max shared by both
@@ -42,15 +44,16 @@ namespace {
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = kConsumerWarps * 32;
 constexpr int kStages = 3;
-constexpr int kSubTile = kBlockTokens * 128;      // 32 rows x 128 B
-constexpr int kEntryBytes = 4 * kSubTile;        // K lo, K hi, V lo, V hi
+constexpr int kRowBytes = kHeadDim * 2;          // one token of one head, FP16
+constexpr int kPlaneBytes = kBlockTokens * kRowBytes;  // 32 rows: 8 KB
+constexpr int kEntryBytes = 2 * kPlaneBytes;     // K plane then V plane
 constexpr int kStageBytes = 2 * kEntryBytes;     // two entries per stage
 constexpr int kPartialStride = 2 + kHeadDim;     // m, l, o[128]
 constexpr int kMaxSplitEntries = 64;
 constexpr unsigned kFull = 0xffffffffu;
 
 template <int G>
-struct alignas(1024) AttnSmem {
+struct alignas(128) AttnSmem {
   uint8_t tiles[kStages][kStageBytes];
   float pbuf[kConsumerWarps][2][4][G];  // probabilities [half][token][head]
   float abuf[kConsumerWarps][G];        // rescale factor per head
@@ -124,12 +127,6 @@ struct Halve {
   }
 };
 
-// Row read of 8 halves (16 B) of token t for a lane at dim-chunk c of a
-// swizzled 32 x 128 B sub-tile.
-__device__ __forceinline__ uint4 row8(const uint8_t* sub, int t, int c) {
-  return *reinterpret_cast<const uint4*>(sub + t * 128 + ((c ^ (t & 7)) << 4));
-}
-
 __device__ __forceinline__ void unpack8(const uint4& u, float2 (&f)[4]) {
   f[0] = h2x2f(u.x);
   f[1] = h2x2f(u.y);
@@ -137,25 +134,29 @@ __device__ __forceinline__ void unpack8(const uint4& u, float2 (&f)[4]) {
   f[3] = h2x2f(u.w);
 }
 
-// Issues the TMA loads of stage j (entries 2j, 2j+1 of the CTA's range).
-template <int G>
-__device__ __forceinline__ void issue_stage(AttnSmem<G>& s, const CUtensorMap* map, int kv_heads,
-                                            int kvh, int n, int j) {
+// Issues the loads of stage j (entries 2j, 2j+1 of the CTA's range): one 16 KB
+// bulk copy per entry from a head-major pool, or two 8 KB TMA tiles per entry
+// from a token-major buffer.
+template <int G, bool kHeadMajor>
+__device__ __forceinline__ void issue_stage(AttnSmem<G>& s, const CUtensorMap* map,
+                                            const uint8_t* pool, int kv_heads, int kvh, int n,
+                                            int j) {
   const int stage = j % kStages;
-  const int x = kvh * kHeadDim;
-  const int xv = kv_heads * kHeadDim + x;
   uint32_t tx = 0;
   for (int e = 2 * j; e < min(n, 2 * j + 2); ++e) tx += s.ent_ntok[e] > 0 ? kEntryBytes : 0;
   if (tx) {
     mbar_arrive_expect_tx(&s.full[stage], tx);
     for (int e = 2 * j; e < min(n, 2 * j + 2); ++e) {
       if (s.ent_ntok[e] <= 0) continue;
-      const int y = s.ent_phys[e] * kBlockTokens;
       uint8_t* dst = s.tiles[stage] + (e & 1) * kEntryBytes;
-      tma_load_2d(dst, map, &s.full[stage], x, y);
-      tma_load_2d(dst + kSubTile, map, &s.full[stage], x + 64, y);
-      tma_load_2d(dst + 2 * kSubTile, map, &s.full[stage], xv, y);
-      tma_load_2d(dst + 3 * kSubTile, map, &s.full[stage], xv + 64, y);
+      if constexpr (kHeadMajor) {
+        bulk_load(dst, pool + ((size_t)s.ent_phys[e] * kv_heads + kvh) * kEntryBytes, kEntryBytes,
+                  &s.full[stage]);
+      } else {
+        const int y = s.ent_phys[e] * kBlockTokens;
+        tma_load_2d(dst, map, &s.full[stage], kvh * kHeadDim, y);
+        tma_load_2d(dst + kPlaneBytes, map, &s.full[stage], (kv_heads + kvh) * kHeadDim, y);
+      }
     }
   } else {
     mbar_arrive(&s.full[stage]);
@@ -163,16 +164,16 @@ __device__ __forceinline__ void issue_stage(AttnSmem<G>& s, const CUtensorMap* m
   s.stage_issues[stage] += 1;
 }
 
-template <int G>
+template <int G, bool kHeadMajor>
 __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
     attention_kernel(const __grid_constant__ CUtensorMap map, const AttnParams p) {
   // Pairs (token, head) per half-warp: 4G over 16 lanes -> VPL per lane.
   constexpr int NPH = 4 * G;
   constexpr int VPL = NPH > 16 ? NPH / 16 : 1;
   constexpr int kPairShift = NPH >= 16 ? 0 : (NPH == 8 ? 1 : 2);  // lanes per pair = 1 << shift
-  extern __shared__ uint8_t smem_raw[];
-  AttnSmem<G>& s = *reinterpret_cast<AttnSmem<G>*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  AttnSmem<G>& s = *reinterpret_cast<AttnSmem<G>*>(smem_raw);
+  const uint8_t* pool = reinterpret_cast<const uint8_t*>(p.pool);
 
   const int unit = blockIdx.y;
   const int split = blockIdx.x;
@@ -201,7 +202,7 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
     }
     s.abort_flag = 0;
     mbar_fence_init();
-    tma_prefetch_desc(&map);
+    if constexpr (!kHeadMajor) tma_prefetch_desc(&map);
   }
   for (int i = threadIdx.x; i < n; i += kThreads) {
     const Entry en = unit_entry(p, sl, sgroup, nsel, tail_len, e_begin + i);
@@ -211,10 +212,10 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
   __syncthreads();
 
   const int half = lane >> 4;      // which entry of the stage
-  const int l16 = lane & 15;
-  const int sub_hi = l16 >> 3;     // dims [0,64) or [64,128)
-  const int chunk = l16 & 7;       // 16 B chunk inside the 128 B row
+  const int l16 = lane & 15;       // 16 B (8 dims) column of a 256 B row
   const int t0 = 4 * warp;
+  // Byte offset of this lane's first K row inside its entry's tile.
+  const int lane_off = half * kEntryBytes + t0 * kRowBytes + l16 * 16;
 
   float m_run[VPL], l_run[VPL];
 #pragma unroll
@@ -229,7 +230,8 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
     for (int c = 0; c < 4; ++c) acc[g][c] = make_float2(0.f, 0.f);
 
   if (threadIdx.x == 0)
-    for (int j = 0; j < min(kStages, nstages); ++j) issue_stage(s, &map, p.kv_heads, kvh, n, j);
+    for (int j = 0; j < min(kStages, nstages); ++j)
+      issue_stage<G, kHeadMajor>(s, &map, pool, p.kv_heads, kvh, n, j);
   {
     // ---------------- every warp consumes ----------------
     // q of this lane's 8 dims for the unit's G heads, pre-scaled into the
@@ -261,15 +263,14 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
       const int e_other = 2 * j + (half ^ 1);
       const int ntok_other = e_other < n ? s.ent_ntok[e_other] : 0;
       if (t0 < ntok || t0 < ntok_other) {
-        const uint8_t* tile = s.tiles[stage] + half * kEntryBytes;
-        const uint8_t* ksub = tile + sub_hi * kSubTile;
-        const uint8_t* vsub = tile + (2 + sub_hi) * kSubTile;
+        const uint8_t* krow = s.tiles[stage] + lane_off;
+        const uint8_t* vrow = krow + kPlaneBytes;
         // ---- QK over this lane's 8 dims, 4 tokens x G heads ----
         float part[NPH];
 #pragma unroll
         for (int tt = 0; tt < 4; ++tt) {
           float2 k[4];
-          unpack8(row8(ksub, t0 + tt, chunk), k);
+          unpack8(*reinterpret_cast<const uint4*>(krow + tt * kRowBytes), k);
 #pragma unroll
           for (int g = 0; g < G; ++g) {
             float2 a = __fmul2_rn(q[g][0], k[0]);
@@ -333,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
         for (int tt = 0; tt < 4; ++tt) {
           if (t0 + tt < ntok) {
             float2 v[4];
-            unpack8(row8(vsub, t0 + tt, chunk), v);
+            unpack8(*reinterpret_cast<const uint4*>(vrow + tt * kRowBytes), v);
             const float* pt = &s.pbuf[warp][half][tt][0];
 #pragma unroll
             for (int g = 0; g < G; ++g) {
@@ -354,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
           __threadfence_block();
           fence_proxy_async_shared();
           if (j + kStages < nstages && !*reinterpret_cast<volatile int*>(&s.abort_flag))
-            issue_stage(s, &map, p.kv_heads, kvh, n, j + kStages);
+            issue_stage<G, kHeadMajor>(s, &map, pool, p.kv_heads, kvh, n, j + kStages);
         }
       }
     }
@@ -476,15 +477,22 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
   if (threadIdx.x == 0) p.counters[unit] = 0;
 }
 
-template <int G>
-sa_status launch_g(const AttnParams& p, const CUtensorMap& map, cudaStream_t stream) {
-  const size_t smem = sizeof(AttnSmem<G>) + 1024;
+template <int G, bool kHeadMajor>
+sa_status launch_layout(const AttnParams& p, const CUtensorMap& map, cudaStream_t stream) {
+  const size_t smem = sizeof(AttnSmem<G>);
   static int configured[kMaxDevices];
-  const sa_status st = ensure_smem_limit((const void*)attention_kernel<G>, (int)smem, configured);
+  const sa_status st =
+      ensure_smem_limit((const void*)attention_kernel<G, kHeadMajor>, (int)smem, configured);
   if (st != SA_OK) return st;
   const dim3 grid(p.max_splits, p.num_sl * p.kv_heads);
-  attention_kernel<G><<<grid, kThreads, smem, stream>>>(map, p);
+  attention_kernel<G, kHeadMajor><<<grid, kThreads, smem, stream>>>(map, p);
   return cuda_status(cudaGetLastError(), "attention_kernel launch");
+}
+
+template <int G>
+sa_status launch_g(const AttnParams& p, const CUtensorMap& map, cudaStream_t stream) {
+  return p.head_major ? launch_layout<G, true>(p, map, stream)
+                      : launch_layout<G, false>(p, map, stream);
 }
 
 }  // namespace

@@ -58,23 +58,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity; false (and SA_DEV_TIMEOUT) if
-// it did not complete within kWaitLimitCycles.
+// it did not complete within kWaitLimitCycles. try_wait itself suspends the
+// thread for a while, so the clock is read only every 16 attempts.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   uint32_t* status) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long start = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - start > kWaitLimitCycles) {
+  for (unsigned i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 15u) == 0 && clock64() - start > kWaitLimitCycles) {
       raise_status(status, SA_DEV_TIMEOUT);
       return false;
     }
   }
-  return true;
 }
 
 // ---- TMA -------------------------------------------------------------------
 
-// 2-D tiled load of box {x extent, y extent} at coordinates (x, y) into
+// 2-D tiled load of the map's box at coordinates (x, y) into
 // shared memory, completing `bar`'s transaction count. No cluster multicast.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int32_t x, int32_t y) {
@@ -89,6 +90,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
 // later async-proxy (TMA) accesses to the same memory.
 __device__ __forceinline__ void fence_proxy_async_shared() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Contiguous bulk copy global -> shared completing `bar`'s transaction count
+// (both addresses 16-byte aligned, bytes a multiple of 16). No multicast.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {

@@ -34,13 +34,15 @@ constexpr int kMaxDevices = 64;
 // ---- TMA descriptors ---------------------------------------------------------
 
 // 2-D tensor map over token rows: x = FP16 element within a row of
-// `row_elems`, y = row. Box {64 elements (128 B), 32 rows}, 128 B swizzle.
+// `row_elems`, y = row. Box {128 elements (256 B), 32 rows}, no swizzle.
 sa_status make_row_tensor_map(CUtensorMap* map, const void* base, uint64_t row_elems,
                               uint64_t rows);
 
 // ---- attention (sa_attention.cu) -----------------------------------------------
 
 struct AttnParams {
+  const void* pool;      // head-major pool base (used when head_major)
+  int head_major;        // 1: [block][KV head][K,V][32][128]; 0: token rows via the map
   int kv_heads;          // KV heads in a pool row
   int group;             // query heads per KV head (1, 2, 4, 8)
   int num_sl;            // (sequence, layer) pairs
@@ -101,8 +103,10 @@ sa_status launch_select(const SelectParams& p, cudaStream_t stream);
 // ---- representatives, append, seal (sa_lifecycle.cu) ------------------------------
 
 struct RepParams {
-  // keys: row r of token p at kv + row_of(p) * row_stride + kv_head * d
+  // keys of token p: token-major kv + row_of(p) * row_stride + kv_head * d, or
+  // (head_major) the K plane of block row_of(p) / 32, head kv_head, row p % 32
   const uint16_t* kv;
+  int head_major;
   int64_t row_stride;       // elements between token rows
   const int32_t* table;     // null -> row_of(p) = p; else table[table_offset + p/32]*32 + p%32
   int table_offset;
@@ -127,8 +131,8 @@ sa_status launch_build_reps(const RepParams& p, cudaStream_t stream);
 sa_status launch_build_reps_per_block(const RepParams& p, cudaStream_t stream);
 
 struct CtxDev {
-  uint16_t* pool;
-  int64_t row_elems;   // 2 * kv_heads * 128
+  uint16_t* pool;      // head-major: [pool_blocks][kv_heads][K,V][32][128]
+  int64_t row_elems;   // 2 * kv_heads * 128 (one token of every head)
   int pool_blocks;
   float* reps;         // [num_sl][qh][128][reps_cap]
   int reps_cap;        // table_blocks rounded up to a multiple of 4

@@ -46,6 +46,8 @@ struct RepCall {
   int tokens;            // T of the call
   int block;             // block within the call
   const uint16_t* kv;
+  int head_major;        // kv is a head-major pool [block][kv_heads][K,V][32][d]
+  int kv_heads;
   int64_t row_stride;
   int kv_head;
   int d;
@@ -70,6 +72,10 @@ __device__ __forceinline__ const uint16_t* key_row(const RepCall& c, int token) 
     row = c.row_base + token;
   }
   if (row < 0 || (c.pool_rows > 0 && row >= c.pool_rows)) return nullptr;
+  if (c.head_major) {
+    const int64_t blk = row / kBlockTokens;
+    return c.kv + ((blk * c.kv_heads + c.kv_head) * 2 * kBlockTokens + row % kBlockTokens) * c.d;
+  }
   return c.kv + row * c.row_stride + (int64_t)c.kv_head * c.d;
 }
 
@@ -181,6 +187,8 @@ __global__ void __launch_bounds__(kRepThreads) reps_kernel(const RepParams p, in
   c.tokens = call_tokens;
   c.block = per_block ? 0 : b;
   c.kv = p.kv;
+  c.head_major = p.head_major;
+  c.kv_heads = p.kv_heads;
   c.row_stride = p.row_stride;
   c.kv_head = h / group;
   c.d = p.d;
@@ -210,6 +218,8 @@ __global__ void __launch_bounds__(kRepThreads) seal_rebuild_kernel(const CtxDev 
       r.tokens = kBlockTokens;
       r.block = 0;
       r.kv = c.pool;
+      r.head_major = 1;
+      r.kv_heads = c.kv_heads;
       r.row_stride = c.row_elems;
       r.kv_head = h / (c.qh / c.kv_heads);
       r.d = kHeadDim;
@@ -267,8 +277,9 @@ __global__ void __launch_bounds__(256) seal_commit_kernel(const CtxDev c) {
   if (threadIdx.x == 0) *c.free_top = max(0, base_top - taken_before);
 }
 
-// grid num_sl: write the current token's K/V into its tail row and its
-// query into the tail's query ring.
+// grid num_sl: write the current token's K/V into its tail row (one row of
+// each KV head's K and V planes of the head-major tail block) and its query
+// into the tail's query ring.
 __global__ void __launch_bounds__(256)
     append_kernel(const CtxDev c, const float* query, const void* kv_new, int kv_fp32) {
   const int sl = blockIdx.x;
@@ -282,19 +293,33 @@ __global__ void __launch_bounds__(256)
     if (threadIdx.x == 0) raise_status(c.status, SA_DEV_BAD_BLOCK);
     return;
   }
+  // Input row [2 (K,V)][kv_heads][128]; plane (kv, h) lands at
+  // ((phys * kv_heads + h) * 2 + kv) * 32 + tl rows of 128 halves.
   const int64_t n = c.row_elems;
-  uint16_t* row = c.pool + ((int64_t)phys * kBlockTokens + tl) * n;
+  uint16_t* block = c.pool + (int64_t)phys * c.kv_heads * 2 * kBlockTokens * kHeadDim;
   if (kv_fp32) {
     const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(kv_new) + sl * n);
     for (int64_t i = threadIdx.x; i < n / 4; i += blockDim.x) {
+      const int64_t e = 4 * i;
+      const int kv = (int)(e / (c.kv_heads * kHeadDim));
+      const int h = (int)(e / kHeadDim) % c.kv_heads;
+      const int d = (int)(e % kHeadDim);
       const float4 v = src[i];
       const uint32_t lo = (uint32_t)f2h_rn(v.x) | ((uint32_t)f2h_rn(v.y) << 16);
       const uint32_t hi = (uint32_t)f2h_rn(v.z) | ((uint32_t)f2h_rn(v.w) << 16);
-      reinterpret_cast<uint2*>(row)[i] = make_uint2(lo, hi);
+      *reinterpret_cast<uint2*>(block + (((int64_t)h * 2 + kv) * kBlockTokens + tl) * kHeadDim + d) =
+          make_uint2(lo, hi);
     }
   } else {
     const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(kv_new) + sl * n);
-    for (int64_t i = threadIdx.x; i < n / 8; i += blockDim.x) reinterpret_cast<uint4*>(row)[i] = src[i];
+    for (int64_t i = threadIdx.x; i < n / 8; i += blockDim.x) {
+      const int64_t e = 8 * i;
+      const int kv = (int)(e / (c.kv_heads * kHeadDim));
+      const int h = (int)(e / kHeadDim) % c.kv_heads;
+      const int d = (int)(e % kHeadDim);
+      *reinterpret_cast<uint4*>(block + (((int64_t)h * 2 + kv) * kBlockTokens + tl) * kHeadDim + d) =
+          src[i];
+    }
   }
   float* ring = c.query_ring + (int64_t)sl * c.qh * kBlockTokens * kHeadDim;
   const float* q = query + (int64_t)sl * c.qh * kHeadDim;

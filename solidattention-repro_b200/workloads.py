@@ -115,7 +115,7 @@ def make_context(w: Workload, decode_steps: int, device: torch.device, seed: int
                         torch.arange(BLOCK, device=device)[None, :]).reshape(-1)
                 k = kv[rows, 0, h - kh0].float() + 0.5 * q_hat
                 kv[rows, 0, h - kh0] = k.half()
-            ctx.pool[base:base + nb] = kv.view(nb, BLOCK, 2, khn, D)
+            ctx.pool[base:base + nb] = kv.view(nb, BLOCK, 2, khn, D).permute(0, 3, 2, 1, 4)
             del kv
             gen.manual_seed(seed * 1000003 + (s * w.layers + layer) * 7919 + 2)
             pq = torch.randn(w.query_heads, nb * BLOCK, D, device=device, generator=gen).half().float()

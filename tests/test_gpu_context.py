@@ -71,8 +71,7 @@ def test_decode_steps_with_seal_match_oracle(pkg, port, cuda, qh, kh, out_fp16):
     for s in range(seqs):
         for l in range(layers):
             phys = ctx.prefill(s, l, nb0)
-            idx = torch.as_tensor(phys[:nb0], dtype=torch.long, device=cuda)
-            ctx.pool[idx] = torch.randn(nb0, 32, 2, kh, D, generator=g).half().to(cuda)
+            ctx.write_blocks(phys[:nb0], torch.randn(nb0, 32, 2, kh, D, generator=g).half())
             pq = torch.randn(qh, nb0 * 32, D, generator=g).half().float().to(cuda)
             ctx.build_reps(s, l, 0, nb0, pq)
     ctx.sync()
@@ -85,7 +84,7 @@ def test_decode_steps_with_seal_match_oracle(pkg, port, cuda, qh, kh, out_fp16):
         tail_before = ctx.tail_block.cpu().numpy().copy()
         out = ctx.step(torch.from_numpy(q).to(cuda), torch.from_numpy(kvn).to(cuda))
         ctx.sync()
-        pool = ctx.pool.cpu().numpy().view(np.uint16)
+        pool = ctx.read_blocks(np.arange(ctx.pool.shape[0])).cpu().numpy().view(np.uint16)
         table = ctx.table.cpu().numpy()
         reps = ctx.reps.cpu().numpy()
         sel = ctx.selected.cpu().numpy()
@@ -151,7 +150,7 @@ def test_lifecycle_bytes_follow_reference_formula(pkg, port, cuda):
     assert ctx.status_bits() & ~pkg.SA_DEV_NONFINITE == 0
     res = port.lifecycle_run(layers, qh, kh, D, 32, 32, decode, 0, with_store=True)
     store = res["store"].reshape(layers, res["capacity_blocks"], 32, tv)
-    pool = ctx.pool.cpu().numpy().view(np.uint16).reshape(-1, 32, tv)
+    pool = ctx.read_blocks(np.arange(ctx.pool.shape[0])).cpu().numpy().view(np.uint16).reshape(-1, 32, tv)
     table = ctx.table.cpu().numpy()
     nb = ctx.num_sealed.cpu().numpy()
     gen = ctx.generation.cpu().numpy()
