@@ -137,7 +137,7 @@ struct sa_ctx {
   int* select_counters = nullptr;
   float* attn_partial = nullptr;
   int* attn_counters = nullptr;
-  int attn_splits = 1, attn_split_entries = 1;
+  AttnPlan attn_plan{};
   // staging for sa_ctx_step_host
   float* d_query = nullptr;
   void* d_kv_new = nullptr;
@@ -172,11 +172,10 @@ SA_API const char* sa_version(void) { return "sa_b200 0.1 sm_100a"; }
 SA_API size_t sa_attention_workspace_size(size_t tokens, size_t query_heads, size_t kv_heads) {
   if (kv_heads == 0 || query_heads % kv_heads != 0) return 0;
   const int entries = (int)((tokens + kBlockTokens - 1) / kBlockTokens);
-  int split = 1;
   const int units = (int)kv_heads;
-  const int nsplit = attention_plan_splits(units, std::max(entries, 1), &split);
-  return attention_scratch_bytes(units, nsplit, (int)(query_heads / kv_heads)) +
-         (size_t)units * sizeof(int) + 256;
+  const int group = (int)(query_heads / kv_heads);
+  const AttnPlan plan = attention_plan(units, std::max(entries, 1), group);
+  return attention_scratch_bytes(plan, units, group) + (size_t)units * sizeof(int) + 256;
 }
 
 SA_API sa_status sa_attention_packed(const uint16_t* kv, const float* query, size_t tokens,
@@ -220,14 +219,16 @@ SA_API sa_status sa_attention_packed(const uint16_t* kv, const float* query, siz
   p.out = out;
   p.out_fp16 = out_fp16;
   p.scale_log2 = scale * 1.4426950408889634f;
-  p.max_splits = attention_plan_splits(units, entries, &p.split_entries);
+  const AttnPlan plan = attention_plan(units, entries, p.group);
+  p.slots_per_unit = plan.slots_per_unit;
+  p.max_segments = plan.max_segments;
+  p.ctas = plan.ctas;
   char* ws = static_cast<char*>(workspace);
-  const size_t partial_bytes = attention_scratch_bytes(units, p.max_splits, p.group);
+  const size_t partial_bytes = attention_scratch_bytes(plan, units, p.group);
   p.partial = reinterpret_cast<float*>(ws);
   p.counters = reinterpret_cast<int*>(ws + ((partial_bytes + 255) & ~size_t(255)));
   p.status = nullptr;
-  if (p.max_splits > 1)
-    SA_CUDA_TRY(cudaMemsetAsync(p.counters, 0, (size_t)units * sizeof(int), s));
+  SA_CUDA_TRY(cudaMemsetAsync(p.counters, 0, (size_t)units * sizeof(int), s));
   return launch_attention(p, map, s);
 }
 
@@ -666,8 +667,9 @@ sa_status ctx_attend(sa_ctx* c, const float* query, void* out) {
   p.out = out;
   p.out_fp16 = c->cfg.out_fp16;
   p.scale_log2 = c->cfg.scale * 1.4426950408889634f;
-  p.split_entries = c->attn_split_entries;
-  p.max_splits = c->attn_splits;
+  p.slots_per_unit = c->attn_plan.slots_per_unit;
+  p.max_segments = c->attn_plan.max_segments;
+  p.ctas = c->attn_plan.ctas;
   p.partial = c->attn_partial;
   p.counters = c->attn_counters;
   p.status = c->dev.status;
@@ -709,7 +711,7 @@ SA_API sa_status sa_ctx_create(const sa_ctx_config* config, sa_ctx** out) {
   d.rep_topk = g.rep_topk;
   d.rep_scale = 1.0f / std::sqrt((float)kHeadDim);
   const int units = c->num_sl * g.kv_heads;
-  c->attn_splits = attention_plan_splits(units, g.budget_blocks + 1, &c->attn_split_entries);
+  c->attn_plan = attention_plan(units, g.budget_blocks + 1, c->group);
 
   st = cuda_status(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "cudaStreamCreate");
   c->own_stream = st == SA_OK;
@@ -732,7 +734,7 @@ SA_API sa_status sa_ctx_create(const sa_ctx_config* config, sa_ctx** out) {
   if (st == SA_OK) st = dalloc(&c->select_counters, nsl * c->n_sel_groups);
   if (st == SA_OK)
     st = dalloc(reinterpret_cast<char**>(&c->attn_partial),
-                attention_scratch_bytes(units, c->attn_splits, c->group));
+                attention_scratch_bytes(c->attn_plan, units, c->group));
   if (st == SA_OK) st = dalloc(&c->attn_counters, (size_t)units);
   if (st == SA_OK) st = dalloc(&c->d_query, nsl * g.query_heads * kHeadDim);
   if (st == SA_OK) st = dalloc(reinterpret_cast<float**>(&c->d_kv_new), nsl * row_elems);

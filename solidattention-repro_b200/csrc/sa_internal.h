@@ -66,16 +66,24 @@ struct AttnParams {
   void* out;           // [num_sl][kv_heads*group][128]
   int out_fp16;
   float scale_log2;     // softmax scale * log2(e)
-  int split_entries;    // entries (blocks) per CTA
-  int max_splits;       // grid.x
-  float* partial;       // [units][max_splits][group][2 + 128]
+  int slots_per_unit;   // entry slots of every unit (selected blocks + tail)
+  int max_segments;     // CTAs that may cover one unit (partials per unit)
+  int ctas;             // grid size
+  float* partial;       // [units][max_segments][group][2 + 128]
   int* counters;        // [units], zero between launches
   uint32_t* status;
 };
 
-// Entries a unit can hold at most (selected blocks + tail).
-int attention_plan_splits(int units, int max_entries, int* split_entries);
-size_t attention_scratch_bytes(int units, int max_splits, int group);
+// The persistent attention schedule: `ctas` CTAs, each owning a contiguous
+// range of the flattened (unit, slot) list; a unit is covered by at most
+// `max_segments` of them.
+struct AttnPlan {
+  int slots_per_unit;
+  int max_segments;
+  int ctas;
+};
+AttnPlan attention_plan(int units, int slots_per_unit, int group);
+size_t attention_scratch_bytes(const AttnPlan& plan, int units, int group);
 sa_status launch_attention(const AttnParams& p, const CUtensorMap& map, cudaStream_t stream);
 
 // ---- selection (sa_select.cu) ----------------------------------------------------
