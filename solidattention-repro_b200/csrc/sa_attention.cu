@@ -55,25 +55,27 @@ constexpr int kPlaneBytes = kBlockTokens * kRowBytes;   // 32 rows: 8 KB
 constexpr int kEntryBytes = 2 * kPlaneBytes;            // K plane then V plane
 constexpr int kStageBytes = 2 * kEntryBytes;            // two entries per stage
 constexpr int kPartialStride = 2 + kHeadDim;            // m, l, o[128]
-constexpr int kMaxCtaSlots = 256;                       // slots one CTA may own
+constexpr int kMaxCtaSlots = 512;                       // slots one CTA may own
 constexpr int kMaxSegments = 32;                        // units one CTA may touch
 constexpr int kSms = 148;                               // B200
 constexpr unsigned kFull = 0xffffffffu;
+constexpr float kLazyRescale = 8.f;                     // log2 units
 
 constexpr int kMaxStages = kMaxCtaSlots / 2 + kMaxSegments;
 
-// Stage table word: tokens of the stage's two entries, its first CTA-local
-// slot, its segment, and whether it opens / closes the segment.
-constexpr uint32_t kInfoStart = 1u << 29;
-constexpr uint32_t kInfoEnd = 1u << 30;
+// Stage table word: tokens of the stage's two entries (6 bits each), its
+// first CTA-local slot (9 bits), its segment (5 bits), and whether it opens /
+// closes the segment.
+constexpr uint32_t kInfoStart = 1u << 26;
+constexpr uint32_t kInfoEnd = 1u << 27;
 __host__ __device__ constexpr uint32_t stage_word(int ntok0, int ntok1, int e0, int seg,
                                                    bool start, bool end) {
-  return (uint32_t)ntok0 | ((uint32_t)ntok1 << 8) | ((uint32_t)e0 << 16) |
-         ((uint32_t)seg << 24) | (start ? kInfoStart : 0u) | (end ? kInfoEnd : 0u);
+  return (uint32_t)ntok0 | ((uint32_t)ntok1 << 6) | ((uint32_t)e0 << 12) |
+         ((uint32_t)seg << 21) | (start ? kInfoStart : 0u) | (end ? kInfoEnd : 0u);
 }
-__device__ __forceinline__ int info_ntok(uint32_t w, int i) { return (w >> (8 * i)) & 0xff; }
-__device__ __forceinline__ int info_e0(uint32_t w) { return (w >> 16) & 0xff; }
-__device__ __forceinline__ int info_seg(uint32_t w) { return (w >> 24) & 0x1f; }
+__device__ __forceinline__ int info_ntok(uint32_t w, int i) { return (w >> (6 * i)) & 0x3f; }
+__device__ __forceinline__ int info_e0(uint32_t w) { return (w >> 12) & 0x1ff; }
+__device__ __forceinline__ int info_seg(uint32_t w) { return (w >> 21) & 0x1f; }
 
 template <int G>
 struct alignas(128) AttnSmem {
@@ -86,7 +88,7 @@ struct alignas(128) AttnSmem {
   float cta_m[G];
   float cta_l[G];
   int ent_phys[kMaxCtaSlots];
-  int ent_ntok[kMaxCtaSlots];
+  uint8_t ent_ntok[kMaxCtaSlots];
   uint32_t stage_info[kMaxStages];
   int seg_slot0[kMaxSegments + 1];   // first CTA-local slot of each segment
   int seg_stage0[kMaxSegments + 1];  // first stage of each segment
@@ -308,7 +310,10 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
     nsel = max(0, min(nsel, p.sel_ids ? p.sel_stride : nsel));
     int tail_len = p.tail_len ? p.tail_len[sl] : p.fixed_tail_len;
     tail_len = max(0, min(tail_len, kBlockTokens));
-    unit_entry(p, sl, sgroup, nsel, tail_len, e, &s.ent_phys[i], &s.ent_ntok[i]);
+    int phys, ntok;
+    unit_entry(p, sl, sgroup, nsel, tail_len, e, &phys, &ntok);
+    s.ent_phys[i] = phys;
+    s.ent_ntok[i] = (uint8_t)ntok;
   }
   __syncthreads();
   if (threadIdx.x < s.nseg) {
@@ -340,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
   // Byte offsets of this lane's 16 B column in its entry's K plane, per token.
   const int col_off = half * kEntryBytes + t0 * kRowBytes + l16 * 16;
 
-  float m_run[VPL], l_run[VPL];
+  float m_run[VPL], m_thr[VPL], l_run[VPL];
   float2 acc[G][4];
   float2 q[G][4];  // q[g] holds head g ^ gsw
   int stage = 0;
@@ -366,6 +371,7 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
 #pragma unroll
       for (int i = 0; i < VPL; ++i) {
         m_run[i] = -INFINITY;
+        m_thr[i] = -INFINITY;
         l_run[i] = 0.f;
       }
     }
@@ -401,36 +407,41 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
         for (int off = 1 << (kPairShift - 1); off >= 1; off >>= 1)
           part[0] += __shfl_xor_sync(kFull, part[0], off);
       }
-      // ---- online softmax: 8 tokens (4 per half-warp) per head ----
-      float pr[VPL], alpha[VPL];
-      bool moved = false;
+      // ---- online softmax over 8 tokens (4 per half-warp) per head, lazily
+      // rescaled: the running max moves only when a logit exceeds it by more
+      // than kLazyRescale (log2 units), so probabilities stay below
+      // 2^kLazyRescale and most stages skip the max reduction and rescale ----
+      float x[VPL];
+      bool over = false;
 #pragma unroll
       for (int i = 0; i < VPL; ++i) {
         const int tt = (pair0 + i) / G;
-        const float x = (t0 + tt < ntok) ? part[i] : -INFINITY;
-        float bm = fmaxf(x, __shfl_xor_sync(kFull, x, 4));
-        bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 8));
-        bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 16));
-        const float m_new = fmaxf(m_run[i], bm);
-        alpha[i] = 1.f;
-        pr[i] = 0.f;
-        if (m_new != -INFINITY) {
-          alpha[i] = fast_exp2(m_run[i] - m_new);
-          pr[i] = fast_exp2(x - m_new);
-        }
-        moved |= m_new != m_run[i];
-        m_run[i] = m_new;
-        l_run[i] = l_run[i] * alpha[i] + pr[i];
+        x[i] = (t0 + tt < ntok) ? part[i] : -INFINITY;
+        over |= x[i] > m_thr[i];
       }
-      if (pair_writer) {
+      const bool rescale = __any_sync(kFull, over);
+      if (rescale) {
 #pragma unroll
         for (int i = 0; i < VPL; ++i) {
+          float bm = fmaxf(x[i], __shfl_xor_sync(kFull, x[i], 4));
+          bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 8));
+          bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 16));
+          const float m_new = fmaxf(m_run[i], bm);
+          const float alpha = m_new == -INFINITY ? 1.f : fast_exp2(m_run[i] - m_new);
+          m_run[i] = m_new;
+          m_thr[i] = m_new + kLazyRescale;
+          l_run[i] *= alpha;
           const int v = pair0 + i;
-          s.pbuf[warp][half][v / G][v % G] = make_float2(pr[i], pr[i]);
-          if (half == 0 && v / G == 0) s.abuf[warp][v % G] = make_float2(alpha[i], alpha[i]);
+          if (pair_writer && half == 0 && v / G == 0) s.abuf[warp][v % G] = make_float2(alpha, alpha);
         }
       }
-      const bool rescale = __any_sync(kFull, moved);
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) {
+        const float pr = x[i] == -INFINITY ? 0.f : fast_exp2(x[i] - m_run[i]);
+        l_run[i] += pr;
+        const int v = pair0 + i;
+        if (pair_writer) s.pbuf[warp][half][v / G][v % G] = make_float2(pr, pr);
+      }
       __syncwarp();
       // ---- PV over the half-warp's 4 tokens ----
       if (rescale) {
@@ -525,12 +536,15 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
             part[g * kPartialStride + 1] = s.cta_l[g];
           }
         }
-        __threadfence();
         __syncthreads();
-        if (threadIdx.x == 0) s.last_flag = atomicAdd(&p.counters[u], 1) == nparts - 1;
+        if (threadIdx.x == 0) {
+          // the barrier orders the CTA's partial stores before this fence
+          __threadfence();
+          s.last_flag = atomicAdd(&p.counters[u], 1) == nparts - 1;
+          if (s.last_flag) __threadfence();
+        }
         __syncthreads();
         if (s.last_flag) {
-          __threadfence();
           const float* parts = p.partial + (size_t)u * p.max_segments * G * kPartialStride;
           for (int idx = threadIdx.x; idx < G * kHeadDim; idx += kThreads) {
             const int g = idx / kHeadDim, d = idx % kHeadDim;
@@ -600,20 +614,60 @@ sa_status launch_g(const AttnParams& p, const CUtensorMap& map, cudaStream_t str
 }  // namespace
 
 AttnPlan attention_plan(int units, int slots_per_unit, int group) {
+  const long long E = std::max(1, slots_per_unit);
+  const long long U = std::max(1, units);
+  const long long total = U * E;
+  const long long wave = (long long)kSms * (group <= 4 ? 2 : 1);  // resident CTAs
+  // Estimated time of a CTA count, in stage times (two slots per stage): the
+  // CTAs run in ceil(C / wave) waves; a segment end (the 8-warp merge) costs
+  // about three stages, and a unit split over n CTAs 2 + n/8 more (its
+  // partials and their merge by the last CTA).
+  auto cost = [&](long long C) -> double {
+    if (C < 1 || C > total) return 1e30;
+    const long long per = (total + C - 1) / C;
+    if (per > kMaxCtaSlots) return 1e30;
+    long long segs, stages;
+    bool split;
+    if (C % U == 0) {  // k CTAs per unit, ranges aligned to units
+      segs = 1;
+      stages = (per + 1) / 2;
+      split = C > U;
+    } else if (U % C == 0) {  // k whole units per CTA
+      segs = U / C;
+      stages = segs * ((E + 1) / 2);
+      split = false;
+    } else {
+      segs = (per + E - 2) / E + 1;
+      stages = (per + 1) / 2 + segs - 1;
+      split = true;
+    }
+    if (segs > kMaxSegments) return 1e30;
+    const long long waves = (C + wave - 1) / wave;
+    const double parts = split ? (double)((E + per - 1) / per + 1) : 0.0;
+    return (double)waves * (double)(stages + 3 * segs) + (split ? 2.0 + parts / 8.0 : 0.0);
+  };
+  long long best = 0;
+  double best_cost = 1e30;
+  auto consider = [&](long long C) {
+    const double c = cost(C);
+    if (c < best_cost || (c == best_cost && C < best)) {
+      best_cost = c;
+      best = C;
+    }
+  };
+  for (long long k = 1; k <= 64; ++k) consider(U * k);
+  for (long long k = 2; k <= kMaxSegments; ++k)
+    if (U % k == 0) consider(U / k);
+  for (long long w = 1; w <= 8; ++w) {
+    const long long per = (total + wave * w - 1) / (wave * w);
+    consider((total + per - 1) / per);
+  }
+  if (best == 0) best = (total + kMaxCtaSlots - 1) / kMaxCtaSlots;  // always feasible
   AttnPlan plan{};
-  plan.slots_per_unit = std::max(1, slots_per_unit);
-  const long long E = plan.slots_per_unit;
-  const long long total = (long long)std::max(units, 1) * E;
-  // One wave of resident CTAs (two per SM up to four heads per KV head),
-  // 2..kMaxCtaSlots slots per CTA, at most kMaxSegments units per CTA.
-  const long long wave = (long long)kSms * (group <= 4 ? 2 : 1);
-  long long per_cta = (total + wave - 1) / wave;
-  per_cta = std::max<long long>(per_cta, 2);
-  per_cta = std::min<long long>(per_cta, kMaxCtaSlots);
-  per_cta = std::min<long long>(per_cta, (kMaxSegments - 2) * E);
-  plan.ctas = (int)((total + per_cta - 1) / per_cta);
+  plan.slots_per_unit = (int)E;
+  plan.ctas = (int)best;
   // every CTA owns at least floor(total / ctas) slots
-  const long long min_slots = std::max<long long>(1, total / plan.ctas);
+  const long long min_slots = std::max<long long>(1, total / best);
   plan.max_segments = (int)((E + min_slots - 1) / min_slots + 1);
   return plan;
 }
