@@ -8,9 +8,13 @@
 // Scoring keeps the reference's floating-point order exactly: per head a
 // sequential head_dim dot product with separately rounded multiply and add
 // (no FMA), divided by the group size and added to the block's score head by
-// head. Each thread owns 4 consecutive blocks, so with dimension-major
-// representatives ([head][dim][block]) a warp's loads of one dim are 512
-// contiguous bytes. Scores are therefore bit-identical to the reference's.
+// head. A CTA covers 128 (or, for groups under four heads, 256 or 512)
+// consecutive blocks; its four warps compute different heads' dot products
+// in parallel, each lane owning 4 consecutive blocks, so with
+// dimension-major representatives ([head][dim][block]) a warp's loads of one
+// dim are 512 contiguous bytes. The per-head dots meet in shared memory and
+// each block's score adds them in head order. Scores are therefore
+// bit-identical to the reference's.
 //
 // Top-k: the reference forces [0, init) and the last `local` blocks, then
 // stable-sorts by descending score and fills up to the budget, returning ids
@@ -30,9 +34,11 @@ namespace sa {
 namespace {
 
 constexpr int kThreads = 128;
-constexpr int kBlocksPerThread = 4;
-constexpr int kChunk = kThreads * kBlocksPerThread;  // blocks per CTA
+constexpr int kWarps = kThreads / 32;
+constexpr int kLaneBlocks = 4;                      // consecutive blocks per lane
+constexpr int kWarpBlocks = 32 * kLaneBlocks;       // 128 blocks per warp pass
 constexpr int kMaxBlocks = 16384;
+constexpr int kDimUnroll = 8;
 constexpr unsigned kFull = 0xffffffffu;
 
 struct TopkShared {
@@ -47,90 +53,125 @@ __device__ __forceinline__ float dot_step(float acc, float q, float r) {
   return __fadd_rn(acc, __fmul_rn(q, r));
 }
 
+// Warps per head and block sub-chunks of a CTA: with fewer than four heads
+// per group the spare warps take further 128-block sub-chunks.
+__host__ __device__ __forceinline__ int heads_per_pass(int group) { return group < kWarps ? group : kWarps; }
+__host__ __device__ __forceinline__ int sub_chunks(int group) { return kWarps / heads_per_pass(group); }
+
+// One head's dot products for the lane's 4 consecutive blocks b0..b0+3, in
+// the reference's order (sequential over dims, multiply and add rounded
+// separately).
+__device__ __forceinline__ void head_dots(const SelectParams& p, const float* rh, const float* qj,
+                                          int b0, int nb, int vec, float (&dot)[kLaneBlocks]) {
+#pragma unroll
+  for (int k = 0; k < kLaneBlocks; ++k) dot[k] = 0.f;
+  if (vec) {
+    const float* col = rh + b0;
+    int dd = 0;
+    for (; dd + kDimUnroll <= p.d; dd += kDimUnroll) {
+      float4 r[kDimUnroll];
+#pragma unroll
+      for (int u = 0; u < kDimUnroll; ++u)
+        r[u] = __ldg(reinterpret_cast<const float4*>(col + (size_t)(dd + u) * p.s_dim));
+#pragma unroll
+      for (int u = 0; u < kDimUnroll; ++u) {
+        const float q = qj[dd + u];
+        dot[0] = dot_step(dot[0], q, r[u].x);
+        dot[1] = dot_step(dot[1], q, r[u].y);
+        dot[2] = dot_step(dot[2], q, r[u].z);
+        dot[3] = dot_step(dot[3], q, r[u].w);
+      }
+    }
+    for (; dd < p.d; ++dd) {
+      const float4 r = __ldg(reinterpret_cast<const float4*>(col + (size_t)dd * p.s_dim));
+      const float q = qj[dd];
+      dot[0] = dot_step(dot[0], q, r.x);
+      dot[1] = dot_step(dot[1], q, r.y);
+      dot[2] = dot_step(dot[2], q, r.z);
+      dot[3] = dot_step(dot[3], q, r.w);
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < kLaneBlocks; ++k) {
+      if (b0 + k >= nb) break;
+      const float* rb = rh + (size_t)(b0 + k) * p.s_block;
+      float acc = 0.f;
+      for (int dd = 0; dd < p.d; ++dd) acc = dot_step(acc, qj[dd], __ldg(rb + (size_t)dd * p.s_dim));
+      dot[k] = acc;
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kThreads)
     select_kernel(const SelectParams p, const int vec) {
-  extern __shared__ float qs[];  // [group][d] then [nb_cap] keys
+  // dynamic shared memory: q [group][d], head dots [group][chunk], then (last
+  // CTA) order keys [nb_cap]
+  extern __shared__ float smem[];
   __shared__ TopkShared ts;
   const int unit = blockIdx.y;
   const int sl = unit / p.n_groups;
   const int g = unit - sl * p.n_groups;
   const int nb = max(0, min(p.nb ? p.nb[sl] : p.fixed_nb, p.nb_cap));
-  const int nchunks = max(1, (nb + kChunk - 1) / kChunk);
+  const int hp = heads_per_pass(p.group);
+  const int sub = sub_chunks(p.group);
+  const int chunk = sub * kWarpBlocks;
+  const int nchunks = max(1, (nb + chunk - 1) / chunk);
   if ((int)blockIdx.x >= nchunks) return;
+  float* qs = smem;
+  float* dots = smem + ((p.group * p.d + 3) & ~3);  // 16-byte aligned
 
   const float* qsrc = p.query + ((size_t)sl * p.qh + (size_t)g * p.group) * p.d;
   for (int i = threadIdx.x; i < p.group * p.d; i += kThreads) qs[i] = qsrc[i];
   __syncthreads();
 
-  float* scores = p.scores + (size_t)unit * p.nb_cap;
-  const int b0 = blockIdx.x * kChunk + threadIdx.x * kBlocksPerThread;
-  if (b0 < nb) {
-    float score[kBlocksPerThread] = {0.f, 0.f, 0.f, 0.f};
-    const float divisor = (float)p.group;
-    for (int j = 0; j < p.group; ++j) {
-      const int h = g * p.group + j;
-      const float* rh = p.reps + (size_t)sl * p.s_sl + (size_t)h * p.s_head;
-      const float* qj = qs + j * p.d;
-      float dot[kBlocksPerThread] = {0.f, 0.f, 0.f, 0.f};
-      if (vec) {
-        const float* col = rh + b0;
-        int dd = 0;
-        for (; dd + 8 <= p.d; dd += 8) {
-          float4 r[8];
-#pragma unroll
-          for (int u = 0; u < 8; ++u)
-            r[u] = __ldg(reinterpret_cast<const float4*>(col + (size_t)(dd + u) * p.s_dim));
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const float q = qj[dd + u];
-            dot[0] = dot_step(dot[0], q, r[u].x);
-            dot[1] = dot_step(dot[1], q, r[u].y);
-            dot[2] = dot_step(dot[2], q, r[u].z);
-            dot[3] = dot_step(dot[3], q, r[u].w);
-          }
-        }
-        for (; dd < p.d; ++dd) {
-          const float4 r = __ldg(reinterpret_cast<const float4*>(col + (size_t)dd * p.s_dim));
-          const float q = qj[dd];
-          dot[0] = dot_step(dot[0], q, r.x);
-          dot[1] = dot_step(dot[1], q, r.y);
-          dot[2] = dot_step(dot[2], q, r.z);
-          dot[3] = dot_step(dot[3], q, r.w);
-        }
-      } else {
-#pragma unroll
-        for (int k = 0; k < kBlocksPerThread; ++k) {
-          if (b0 + k >= nb) break;
-          const float* rb = rh + (size_t)(b0 + k) * p.s_block;
-          float acc = 0.f;
-          for (int dd = 0; dd < p.d; ++dd) acc = dot_step(acc, qj[dd], __ldg(rb + (size_t)dd * p.s_dim));
-          dot[k] = acc;
-        }
+  // ---- per-head dot products: warp w takes head w % hp (+ hp, ...) of
+  // sub-chunk w / hp ----
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sc = warp / hp;
+  const int cbase = blockIdx.x * chunk;
+  if (sc < sub) {
+    const int lb = sc * kWarpBlocks + lane * kLaneBlocks;  // chunk-local first block
+    const int b0 = cbase + lb;
+    for (int j = warp % hp; j < p.group; j += hp) {
+      float dot[kLaneBlocks] = {0.f, 0.f, 0.f, 0.f};
+      if (b0 < nb) {
+        const int h = g * p.group + j;
+        head_dots(p, p.reps + (size_t)sl * p.s_sl + (size_t)h * p.s_head, qs + j * p.d, b0, nb,
+                  vec, dot);
       }
-#pragma unroll
-      for (int k = 0; k < kBlocksPerThread; ++k)
-        score[k] = __fadd_rn(score[k], __fdiv_rn(dot[k], divisor));
+      *reinterpret_cast<float4*>(dots + (size_t)j * chunk + lb) =
+          make_float4(dot[0], dot[1], dot[2], dot[3]);
     }
-#pragma unroll
-    for (int k = 0; k < kBlocksPerThread; ++k)
-      if (b0 + k < nb) scores[b0 + k] = score[k];
+  }
+  __syncthreads();
+  // ---- block scores: sum over the group's heads in head order ----
+  float* scores = p.scores + (size_t)unit * p.nb_cap;
+  const float divisor = (float)p.group;
+  for (int lb = threadIdx.x; lb < chunk; lb += kThreads) {
+    const int b = cbase + lb;
+    if (b >= nb) break;
+    float score = 0.f;
+    for (int j = 0; j < p.group; ++j) score = __fadd_rn(score, __fdiv_rn(dots[(size_t)j * chunk + lb], divisor));
+    scores[b] = score;
   }
 
   // ---- the last CTA of this (sl, group) selects ----
+  __syncthreads();
   if (nchunks > 1) {
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) ts.last = atomicAdd(&p.counters[unit], 1) == nchunks - 1;
+    if (threadIdx.x == 0) {
+      // the barrier orders the CTA's score stores before this fence
+      __threadfence();
+      ts.last = atomicAdd(&p.counters[unit], 1) == nchunks - 1;
+      if (ts.last) {
+        __threadfence();
+        p.counters[unit] = 0;
+      }
+    }
     __syncthreads();
     if (!ts.last) return;
-    __threadfence();
-    if (threadIdx.x == 0) p.counters[unit] = 0;
-  } else {
-    __threadfence();
-    __syncthreads();
   }
 
-  uint32_t* keys = reinterpret_cast<uint32_t*>(qs + p.group * p.d);
+  uint32_t* keys = reinterpret_cast<uint32_t*>(smem);  // q and dots are no longer needed
   const int budget = min(p.budget, nb);
   const int n_init = min(p.init, nb);
   const int n_local = min(p.local, nb);
@@ -240,12 +281,15 @@ sa_status launch_select(const SelectParams& p, cudaStream_t stream) {
     return fail(SA_ERR_UNSUPPORTED, "select: more than 65535 (sequence-layer, group) units");
   const int vec = p.s_block == 1 && p.s_dim % 4 == 0 && p.s_head % 4 == 0 && p.s_sl % 4 == 0 &&
                   p.nb_cap % 4 == 0 && (reinterpret_cast<uintptr_t>(p.reps) & 15u) == 0;
-  const size_t smem = ((size_t)p.group * p.d + (size_t)p.nb_cap) * sizeof(float);
+  const int chunk = sub_chunks(p.group) * kWarpBlocks;
+  const size_t smem =
+      std::max((((size_t)p.group * p.d + 3) & ~size_t(3)) + (size_t)p.group * chunk,
+               (size_t)p.nb_cap) * sizeof(float);
   static int configured[kMaxDevices];
   const sa_status st =
       ensure_smem_limit((const void*)select_kernel, (int)std::max<size_t>(smem, 48 * 1024), configured);
   if (st != SA_OK) return st;
-  const int nchunks = std::max(1, (p.nb_cap + kChunk - 1) / kChunk);
+  const int nchunks = std::max(1, (p.nb_cap + chunk - 1) / chunk);
   const dim3 grid(nchunks, p.num_sl * p.n_groups);
   select_kernel<<<grid, kThreads, smem, stream>>>(p, vec);
   return cuda_status(cudaGetLastError(), "select_kernel launch");
