@@ -9,8 +9,11 @@ selected blocks plus the open tail, and seal the tail when it holds 32
 tokens. The default workload is the path's target configuration: Qwen3-8B
 shape (32 query / 8 KV heads, head_dim 128, 36 layers), 32K context (1024
 blocks), 4096-token budget (1 init + 4 local + 123 dynamic blocks). At N > 1
-each rank decodes its own sequence (sequence sharding, no data-path
-collective): weak scaling; value = all ranks' sequence-steps / max time.
+each rank decodes its own sequences (sequence sharding by global batch index,
+no data-path collective): weak scaling; value = all ranks' sequence-steps /
+max time. `--config cfg5` (one 128K-context sequence) shards the KV heads
+instead: rank r holds KH/N heads of every layer, and each step ends with an
+NCCL all-gather of the per-head outputs: strong scaling.
 
 `value` is device-timed with inputs resident in HBM; `e2e` runs the same
 steps through the public host-buffer call (sa_ctx_step_host: H2D of the
@@ -45,7 +48,7 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--config", default="cfg3", choices=["cfg1", "cfg2", "cfg3", "cfg5"])
+    ap.add_argument("--config", default="cfg3", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--kernel-iters", type=int, default=50)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -92,6 +95,18 @@ class ClockSampler:
         except (FileNotFoundError, OSError):
             self.proc = None
 
+    def wait_first(self, timeout: float = 10.0) -> None:
+        """Block until nvidia-smi has printed its first row (its start-up can
+        take longer than a short timed region)."""
+        self.first = ""
+        if self.proc is None or self.proc.stdout is None:
+            return
+        import select
+
+        ready, _, _ = select.select([self.proc.stdout], [], [], timeout)
+        if ready:
+            self.first = self.proc.stdout.readline()
+
     def stop(self):
         if self.proc is None:
             return None
@@ -101,6 +116,7 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
             out, _ = self.proc.communicate()
+        out = getattr(self, "first", "") + (out or "")
         rows = [r.split(",") for r in out.strip().splitlines() if r.count(",") >= 8]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
@@ -190,6 +206,8 @@ def reference_arm(args, w, rank):
     n_sample = 2 if total > 40 else 4
     n_sample = min(n_sample, w.layers)
     nb = w.context_blocks
+    if w.context_min_blocks:
+        nb = int(round(np.mean([w.sequence_blocks(b) for b in range(w.batch)])))
     tail_len = 16
     tv = 2 * w.kv_heads * 128
     pool = (rng.standard_normal((n_sample * (nb + 1) * 32 * tv,), dtype=np.float32)
@@ -271,27 +289,48 @@ def main():
 
     total = args.steps + args.warmup
     e2e_steps = min(args.steps, 500)
+    heads_mode = args.config == "cfg5" and world > 1
+    if heads_mode:
+        # KV-head sharding of one long sequence
+        from solidattention_repro_b200 import sharding
+        kv_slice = sharding.shard_kv_heads(w.kv_heads, world, rank)
+        seq_offset = 0
+    else:
+        kv_slice = None
+        seq_offset = rank * w.seqs  # sequence sharding by global batch index
     # table room for every append of the run: warmup + timed + e2e steps
-    ctx, info = workloads.make_context(w, total + e2e_steps + 64, dev, seed=1 + rank)
+    ctx, info = workloads.make_context(w, total + e2e_steps + 64, dev, seed=1,
+                                       kv_heads_slice=kv_slice, seq_offset=seq_offset)
     phase_bits = {}
-    queries, kv_new = workloads.decode_inputs(w, info, total, dev, seed=1 + rank)
+    queries, kv_new = workloads.decode_inputs(w, info, total, dev, seed=1 + seq_offset,
+                                              kv_heads_slice=kv_slice)
     out = ctx.new_output()
     stream = ctx.stream
+    gathered = None
+    if heads_mode:
+        gathered = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device=dev)
 
-    for s in range(args.warmup):
+    def step(s):
         ctx.step(queries[s], kv_new[s], out)
+        if heads_mode:
+            # [world][S][L][QH/world][D]: rank order = head order
+            dist.all_gather_into_tensor(gathered, out)
+
+    with torch.cuda.stream(stream):
+        for s in range(args.warmup):
+            step(s)
     ctx.sync()
     barrier()
     torch.cuda.synchronize()
     launches0 = ctx.launches
     clocks = ClockSampler(local_rank)
-    time.sleep(0.25)  # the sampler's first sample lands before the region
+    clocks.wait_first()  # the sampler is running before the region starts
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         start.record(stream)
         for s in range(args.warmup, total):
-            ctx.step(queries[s], kv_new[s], out)
+            step(s)
         end.record(stream)
     end.synchronize()
     clock_info = clocks.stop()
@@ -302,7 +341,8 @@ def main():
     barrier()
     torch.cuda.synchronize()
     ms = max_over_ranks(ms_local)
-    steps_per_s = world * w.seqs * args.steps / (ms / 1000.0)
+    seqs_total = w.seqs if heads_mode else world * w.seqs
+    steps_per_s = seqs_total * args.steps / (ms / 1000.0)
 
     # ---- per-kernel roofline: each kernel alone, on its launch stream
     q_last = queries[total - 1]
@@ -310,9 +350,9 @@ def main():
     tail_now = ctx.tail_len.cpu().numpy()
     ctx.select(q_last)
     counts = ctx.selected_count.cpu().numpy()
-    kv_bytes = int(sum((int(counts[sl].max()) * 32 + int(tail_now[sl])) * 2 * w.kv_heads * 128 * 2
+    kv_bytes = int(sum((int(counts[sl].max()) * 32 + int(tail_now[sl])) * 2 * ctx.kh * 128 * 2
                        for sl in range(ctx.num_sl)))
-    rep_bytes = int(sum(int(n) for n in nb_now) * w.query_heads * 128 * 4)
+    rep_bytes = int(sum(int(n) for n in nb_now) * ctx.qh * 128 * 4)
 
     def time_kernel(fn):
         for _ in range(3):
@@ -347,9 +387,27 @@ def main():
                            pin_memory=True)
     q_host.copy_(queries[0].reshape(-1).cpu())
     kv_host.copy_(kv_new[0].reshape(-1).cpu())
+    if heads_mode:
+        # H2D of this rank's query/K/V shard, the device step, the all-gather
+        # of the per-head outputs, D2H of the assembled output
+        q_dev = torch.empty_like(queries[0])
+        kv_dev = torch.empty_like(kv_new[0])
+        out_host = torch.empty(tuple(gathered.shape), dtype=gathered.dtype, pin_memory=True)
+
+        def e2e_step():
+            with torch.cuda.stream(stream):
+                q_dev.copy_(q_host.view_as(q_dev), non_blocking=True)
+                kv_dev.copy_(kv_host.view_as(kv_dev), non_blocking=True)
+                ctx.step(q_dev, kv_dev, out)
+                dist.all_gather_into_tensor(gathered, out)
+                out_host.copy_(gathered, non_blocking=True)
+            stream.synchronize()
+    else:
+        def e2e_step():
+            ctx.step_host(q_host, kv_host, out_host)
     try:
         for _ in range(3):
-            ctx.step_host(q_host, kv_host, out_host)
+            e2e_step()
     finally:
         phase_bits["e2e_warmup"] = ctx.status_bits()
     barrier()
@@ -357,13 +415,13 @@ def main():
     t0 = time.perf_counter()
     try:
         for _ in range(e2e_steps):
-            ctx.step_host(q_host, kv_host, out_host)
+            e2e_step()
     finally:
         phase_bits["e2e"] = ctx.status_bits()
         if any(phase_bits.values()):
             print(json.dumps({"rank": rank, "device_status_bits": phase_bits}), file=sys.stderr)
     e2e_s = max_over_ranks(time.perf_counter() - t0)
-    e2e = {"value": world * w.seqs * e2e_steps / e2e_s, "unit": "steps/s",
+    e2e = {"value": seqs_total * e2e_steps / e2e_s, "unit": "steps/s",
            "h2d_bytes_per_step": q_host.numel() * 4 + kv_host.numel() * 2,
            "d2h_bytes_per_step": out_host.numel() * out_host.element_size() + 4,
            "steps": e2e_steps, "timing": "host wall clock around synchronous calls, max over ranks"}
@@ -376,14 +434,18 @@ def main():
         line = {
             "metric": METRIC, "value": steps_per_s, "unit": "steps/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "strong" if heads_mode else "weak",
+            "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: seeded FP16 N(0,1) KV with planted hot blocks, seeded queries",
             "config": {
                 "workload": w.name, "layers": w.layers, "query_heads": w.query_heads,
                 "kv_heads": w.kv_heads, "head_dim": 128, "context_tokens": w.context_blocks * 32,
                 "budget_blocks": w.budget_blocks, "init_blocks": w.init_blocks,
                 "local_blocks": w.local_blocks, "seqs_per_gpu": w.seqs,
-                "parallelism": f"sequence-sharded x{world}" if world > 1 else "single",
+                "context_min_tokens": (w.context_min_blocks or w.context_blocks) * 32,
+                "parallelism": (f"kv-head-sharded x{world}, NCCL all-gather of outputs per step"
+                                if heads_mode else
+                                f"sequence-sharded x{world}" if world > 1 else "single"),
                 "l2": "inputs larger than L2: each step reads its selected KV and all "
                       "representatives (>1 GB at cfg3)",
                 "kv_dtype": "fp16", "accumulate": "fp32"},

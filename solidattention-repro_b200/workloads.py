@@ -42,6 +42,19 @@ class Workload:
     local_blocks: int
     hot_blocks: int
     out_fp16: bool = True
+    # variable context: when > 0, sequence b's context is a seeded uniform
+    # draw in [context_min_blocks, context_blocks] blocks (context_blocks is
+    # then the maximum); batch = sequences of the whole box
+    context_min_blocks: int = 0
+    batch: int = 1
+
+    def sequence_blocks(self, global_seq: int) -> int:
+        """Sealed blocks of sequence `global_seq` at the start of decoding."""
+        if self.context_min_blocks <= 0:
+            return self.context_blocks
+        tokens = np.random.default_rng(7_000_003 + global_seq).integers(
+            self.context_min_blocks * BLOCK, self.context_blocks * BLOCK + 1)
+        return int(max(self.context_min_blocks, min(self.context_blocks, round(tokens / BLOCK))))
 
     @property
     def group(self) -> int:
@@ -65,43 +78,56 @@ CONFIGS = {
     "cfg2": Workload("cfg2-qwen3-0.6b-28layer-16k-budget2048", 16, 8, 28, 1, 512, 64, 1, 4, 8),
     "cfg3": Workload("cfg3-qwen3-8b-36layer-32k-budget4096", 32, 8, 36, 1, 1024, 128, 1, 4, 16),
     "cfg5": Workload("cfg5-qwen3-8b-36layer-128k-budget8192", 32, 8, 36, 1, 4096, 256, 1, 8, 32),
+    # batch of 64 sequences with 8K..32K contexts, 8 sequences per GPU (the
+    # per-GPU share of the batch on 8 GPUs; the whole batch needs >180 GB)
+    "cfg4": Workload("cfg4-qwen3-8b-36layer-batch64-8k-32k-budget2048", 32, 8, 36, 8, 1024, 64, 1,
+                     4, 0, context_min_blocks=256, batch=64),
 }
 
 
 def make_context(w: Workload, decode_steps: int, device: torch.device, seed: int = 0,
-                 kv_heads_slice: tuple[int, int] | None = None) -> tuple[DecodeContext, dict]:
+                 kv_heads_slice: tuple[int, int] | None = None,
+                 seq_offset: int = 0) -> tuple[DecodeContext, dict]:
     """Build a DecodeContext holding workload `w`, ready for `decode_steps` steps.
 
     kv_heads_slice=(first, count) keeps only those KV heads (and their query
     heads) on this device: the KV-head sharding of a long single sequence.
-    Returns (ctx, info) with the base queries and hot block ids.
+    seq_offset = the global batch index of this context's first sequence
+    (sequence sharding of a batch: context lengths follow the global index).
+    Returns (ctx, info) with the base queries, hot block ids and per-sequence
+    context blocks.
     """
     kh0, khn = kv_heads_slice or (0, w.kv_heads)
     qh = khn * w.group
     extra = decode_steps // BLOCK + 2
-    table_blocks = w.context_blocks + extra
+    seq_nb = [w.sequence_blocks(seq_offset + s) for s in range(w.seqs)]
+    table_blocks = max(seq_nb) + extra
     ctx = DecodeContext(query_heads=qh, kv_heads=khn, layers=w.layers, seqs=w.seqs,
-                        pool_blocks=w.seqs * w.layers * (table_blocks + 1),
+                        pool_blocks=w.layers * sum(nb + extra + 1 for nb in seq_nb),
                         table_blocks=table_blocks, budget_blocks=w.budget_blocks,
                         init_blocks=w.init_blocks, local_blocks=w.local_blocks,
                         out_fp16=w.out_fp16, device=device)
     gen = torch.Generator(device=device)
-    rng = np.random.default_rng(seed)
-    nb = w.context_blocks
-    # base decode queries for the full head set, so a KV-head shard sees the
-    # same values as the unsharded sequence
-    gen.manual_seed(seed * 1000003 + 17)
-    q_base_full = torch.randn(w.seqs, w.layers, w.query_heads, D, device=device,
-                              generator=gen).half().float()
+    # Every draw is seeded by (seed, global sequence index, layer), so a
+    # sequence shard or a KV-head shard sees exactly the values of the
+    # unsharded batch. Base decode queries cover the full head set.
+    q_base_full = torch.empty(w.seqs, w.layers, w.query_heads, D, device=device)
+    for s in range(w.seqs):
+        gen.manual_seed(seed * 1000003 + 17 + 104729 * (seq_offset + s))
+        q_base_full[s] = torch.randn(w.layers, w.query_heads, D, device=device,
+                                     generator=gen).half().float()
     q_base = q_base_full[:, :, kh0 * w.group:(kh0 + khn) * w.group].contiguous()
     hot = np.zeros((w.seqs, w.layers, w.kv_heads, w.hot_blocks), np.int64)
-    candidates = np.arange(w.init_blocks, nb - w.local_blocks)
     for s in range(w.seqs):
+        gs = seq_offset + s
+        nb = seq_nb[s]
+        rng = np.random.default_rng((seed, gs))
+        candidates = np.arange(w.init_blocks, nb - w.local_blocks)
         for layer in range(w.layers):
             phys = ctx.prefill(s, layer, nb)
             base = int(phys[0])
             assert (phys[:nb] == np.arange(base, base + nb)).all()
-            gen.manual_seed(seed * 1000003 + (s * w.layers + layer) * 7919 + 1)
+            gen.manual_seed(seed * 1000003 + (gs * w.layers + layer) * 7919 + 1)
             kv = torch.randn(nb * BLOCK, 2, w.kv_heads, D, device=device, generator=gen).half()
             kv = kv[:, :, kh0:kh0 + khn].contiguous()
             for h in range(w.kv_heads):
@@ -117,13 +143,14 @@ def make_context(w: Workload, decode_steps: int, device: torch.device, seed: int
                 kv[rows, 0, h - kh0] = k.half()
             ctx.pool[base:base + nb] = kv.view(nb, BLOCK, 2, khn, D).permute(0, 3, 2, 1, 4)
             del kv
-            gen.manual_seed(seed * 1000003 + (s * w.layers + layer) * 7919 + 2)
+            gen.manual_seed(seed * 1000003 + (gs * w.layers + layer) * 7919 + 2)
             pq = torch.randn(w.query_heads, nb * BLOCK, D, device=device, generator=gen).half().float()
             pq = pq[kh0 * w.group:(kh0 + khn) * w.group].contiguous()
             ctx.build_reps(s, layer, 0, nb, pq, window=32, topk=4, per_block=True)
             del pq
     ctx.sync()
-    return ctx, {"q_base": q_base, "hot": hot, "qh_local": qh, "kv_heads_local": khn}
+    return ctx, {"q_base": q_base, "hot": hot, "qh_local": qh, "kv_heads_local": khn,
+                 "seq_blocks": seq_nb}
 
 
 def decode_inputs(w: Workload, info: dict, steps: int, device: torch.device, seed: int = 0,

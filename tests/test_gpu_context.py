@@ -177,3 +177,84 @@ def test_pool_exhaustion_sets_status_not_fault(pkg, cuda):
     with pytest.raises(pkg.SparseKVError):
         ctx.sync()
     ctx.close()
+
+
+def test_variable_context_batch_matches_oracle(pkg, port, cuda):
+    """A batch whose sequences hold different numbers of sealed blocks (the
+    batched paged-decode configuration): every (sequence, layer) selects over
+    its own block count and attends over its own table."""
+    qh, kh, layers, budget, init, local = 16, 8, 2, 12, 1, 3
+    seq_nb = [14, 40, 27]
+    seqs = len(seq_nb)
+    rng = np.random.default_rng(5)
+    g = torch.Generator().manual_seed(5)
+    ctx = pkg.DecodeContext(query_heads=qh, kv_heads=kh, layers=layers, seqs=seqs,
+                            pool_blocks=layers * sum(n + 3 for n in seq_nb),
+                            table_blocks=max(seq_nb) + 2, budget_blocks=budget,
+                            init_blocks=init, local_blocks=local, out_fp16=True, device=cuda)
+    for s, nb in enumerate(seq_nb):
+        for l in range(layers):
+            phys = ctx.prefill(s, l, nb)
+            ctx.write_blocks(phys[:nb], torch.randn(nb, 32, 2, kh, D, generator=g).half())
+            ctx.build_reps(s, l, 0, nb, torch.randn(qh, nb * 32, D, generator=g).half().float().to(cuda))
+    ctx.sync()
+    scale = np.float32(1) / np.sqrt(np.float32(D))
+    for step in range(3):
+        q = rng.standard_normal((seqs, layers, qh, D), dtype=np.float32).astype(np.float16).astype(np.float32)
+        kvn = rng.standard_normal((seqs, layers, 2, kh, D), dtype=np.float32).astype(np.float16)
+        nb_before = ctx.num_sealed.cpu().numpy().copy()
+        tail_before = ctx.tail_block.cpu().numpy().copy()
+        out = ctx.step(torch.from_numpy(q).to(cuda), torch.from_numpy(kvn).to(cuda))
+        ctx.sync()
+        assert ctx.status_bits() == 0
+        pool = ctx.read_blocks(np.arange(ctx.pool.shape[0])).cpu().numpy().view(np.uint16)
+        table, reps, sel = ctx.table.cpu().numpy(), ctx.reps.cpu().numpy(), ctx.selected.cpu().numpy()
+        counts = ctx.selected_count.cpu().numpy()
+        got = out.float().cpu().numpy()
+        for s in range(seqs):
+            for l in range(layers):
+                sl = s * layers + l
+                assert nb_before[sl] == seq_nb[s]
+                ids, want = _oracle_step(port, pool, table[sl], nb_before[sl], reps[sl], q[s, l],
+                                         tail_before[sl], step + 1, qh, kh, budget, init, local, scale)
+                assert (counts[sl] == min(budget, seq_nb[s])).all()
+                assert np.array_equal(sel[sl][:, :ids.shape[1]], ids), (step, s, l)
+                err = np.abs(got[s, l] - want).max()
+                assert err <= 2e-3 and cosine(got[s, l], want) >= 0.99999, (step, s, l, err)
+    ctx.close()
+
+
+def test_kv_head_shards_reassemble_the_unsharded_step(pkg, cuda):
+    """KV-head sharding (the long-context multi-GPU layout) on one device: two
+    contexts holding KV heads [0, 4) and [4, 8) of the same sequence select
+    the same blocks per KV head as the unsharded context, and their outputs,
+    concatenated over heads (the all-gather's layout), equal its output."""
+    import dataclasses
+
+    from solidattention_repro_b200 import sharding, workloads
+
+    w = dataclasses.replace(workloads.CONFIGS["cfg2"], name="shard-test", layers=2,
+                            context_blocks=96, budget_blocks=20, hot_blocks=4)
+    full, info = workloads.make_context(w, 8, cuda, seed=3)
+    q, kv = workloads.decode_inputs(w, info, 4, cuda, seed=3)
+    shards = []
+    for r in range(2):
+        sl = sharding.shard_kv_heads(w.kv_heads, 2, r)
+        ctx, inf = workloads.make_context(w, 8, cuda, seed=3, kv_heads_slice=sl)
+        qs, kvs = workloads.decode_inputs(w, inf, 4, cuda, seed=3, kv_heads_slice=sl)
+        shards.append((sl, ctx, qs, kvs))
+    for step in range(4):
+        want = full.step(q[step], kv[step]).float().cpu().numpy()
+        want_ids = full.selected.cpu().numpy()
+        outs = []
+        for (kh0, khn), ctx, qs, kvs in shards:
+            outs.append(ctx.step(qs[step], kvs[step]).float().cpu().numpy())
+            # selection group = one KV head: the shard's groups are the full context's
+            assert np.array_equal(ctx.selected.cpu().numpy(), want_ids[:, kh0:kh0 + khn]), step
+        got = sharding.assemble_heads(outs, w.group)
+        assert got.shape == want.shape
+        assert np.abs(got - want).max() <= 2e-3 and cosine(got.ravel(), want.ravel()) >= 0.999999
+    for _, ctx, _, _ in shards:
+        assert ctx.status_bits() == 0
+        ctx.close()
+    full.close()

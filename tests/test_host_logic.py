@@ -41,6 +41,27 @@ def test_algorithmic_bytes_match_the_configs(workloads):
     assert (c["cfg5"].init_blocks, c["cfg5"].local_blocks, c["cfg5"].budget_blocks) == (1, 8, 256)
 
 
+def test_batched_config_context_draws(workloads):
+    """cfg4: 64 sequences with seeded contexts uniform in [8192, 32768] tokens
+    (whole blocks), a 2048-token budget each, 8 per GPU; a sequence's length
+    depends only on its global batch index, so sequence shards compose."""
+    w = workloads.CONFIGS["cfg4"]
+    assert (w.batch, w.seqs, w.budget_blocks, w.query_heads, w.kv_heads, w.layers) == \
+        (64, 8, 64, 32, 8, 36)
+    nbs = [w.sequence_blocks(b) for b in range(w.batch)]
+    assert nbs == [w.sequence_blocks(b) for b in range(w.batch)]
+    assert all(256 <= n <= 1024 for n in nbs)
+    assert len(set(nbs)) > 32  # genuinely variable
+    # the 8 ranks' shards are the whole batch
+    from solidattention_repro_b200 import sharding
+
+    owned = [sharding.shard_sequences(w.batch, 8, r) for r in range(8)]
+    assert [o[1] for o in owned] == [w.seqs] * 8
+    assert sorted(i for f, n in owned for i in range(f, f + n)) == list(range(w.batch))
+    # fixed-context configs ignore the draw
+    assert workloads.CONFIGS["cfg3"].sequence_blocks(17) == 1024
+
+
 def test_clock_sampler_parses_nvidia_smi_rows(bench):
     s = bench.ClockSampler.__new__(bench.ClockSampler)
 
