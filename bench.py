@@ -53,6 +53,10 @@ def parse_args():
     ap.add_argument("--kernel-iters", type=int, default=50)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
+                    help="KV-head sharding (cfg5, N > 1): gather the per-head outputs with "
+                         "peer-memory stores from the attention kernel (p2p) or an NCCL "
+                         "all-gather after it (nccl)")
     ap.add_argument("--layers", type=int, default=None,
                     help="override the workload's layer count (small profiling cases)")
     return ap.parse_args()
@@ -307,12 +311,19 @@ def main():
     out = ctx.new_output()
     stream = ctx.stream
     gathered = None
+    p2p = heads_mode and args.gather == "p2p"
     if heads_mode:
         gathered = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device=dev)
+        if p2p:
+            ctx.enable_gather(world, rank)
+        barrier()
 
     def step(s):
         ctx.step(queries[s], kv_new[s], out)
-        if heads_mode:
+        if p2p:
+            # the attention kernel stored every output into all ranks' buffers
+            ctx.gather_wait(view=False)
+        elif heads_mode:
             # [world][S][L][QH/world][D]: rank order = head order
             dist.all_gather_into_tensor(gathered, out)
 
@@ -399,8 +410,11 @@ def main():
                 q_dev.copy_(q_host.view_as(q_dev), non_blocking=True)
                 kv_dev.copy_(kv_host.view_as(kv_dev), non_blocking=True)
                 ctx.step(q_dev, kv_dev, out)
-                dist.all_gather_into_tensor(gathered, out)
-                out_host.copy_(gathered, non_blocking=True)
+                if p2p:
+                    out_host.view(-1).copy_(ctx.gather_wait().reshape(-1), non_blocking=True)
+                else:
+                    dist.all_gather_into_tensor(gathered, out)
+                    out_host.copy_(gathered, non_blocking=True)
             stream.synchronize()
     else:
         def e2e_step():
@@ -443,7 +457,9 @@ def main():
                 "budget_blocks": w.budget_blocks, "init_blocks": w.init_blocks,
                 "local_blocks": w.local_blocks, "seqs_per_gpu": w.seqs,
                 "context_min_tokens": (w.context_min_blocks or w.context_blocks) * 32,
-                "parallelism": (f"kv-head-sharded x{world}, NCCL all-gather of outputs per step"
+                "parallelism": (f"kv-head-sharded x{world}, outputs gathered by "
+                                + ("the attention kernel's peer-memory stores (NVLink P2P)"
+                                   if p2p else "an NCCL all-gather") + " every step"
                                 if heads_mode else
                                 f"sequence-sharded x{world}" if world > 1 else "single"),
                 "l2": "inputs larger than L2: each step reads its selected KV and all "

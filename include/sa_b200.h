@@ -313,6 +313,39 @@ SA_API sa_status sa_ctx_sync(sa_ctx* ctx, uint32_t* bits_out);
 /* Kernel launches issued by the context since creation (for accounting). */
 SA_API uint64_t sa_ctx_launch_count(const sa_ctx* ctx);
 
+/* ---- KV-head-sharded contexts: outputs gathered over peer memory ---------
+ * No reference counterpart as a function: replaces the all-gather of
+ * per-head attention outputs that follows the attention when one long
+ * sequence's KV heads are split across `world` GPUs (rank r's context holds
+ * KV heads [r*KH, (r+1)*KH), KH = its kv_heads). Once attached, every
+ * attention launch of the context also stores each (seq-layer, KV head)
+ * output into the current parity slot of every rank's gathered buffer
+ * (NVLink P2P stores), laid out [seqs][layers][world*QH][D] (the full head
+ * set), and counts one system-scope arrival per output on every rank's
+ * buffer. sa_ctx_gather_wait enqueues a bounded wait for all ranks' outputs
+ * of the latest attention. Slots alternate per attention, so a slot stays
+ * valid until the attention after next.
+ *
+ * Setup, per rank: sa_ctx_gather_buffer -> sa_ipc_export the buffer ->
+ * exchange the handles (any host channel) -> sa_ipc_open every other rank's
+ * handle -> sa_ctx_gather_attach with the [world] pointers (own buffer at
+ * index rank). Every rank's context must have the same shape. */
+#define SA_IPC_HANDLE_BYTES 64
+/* Allocate (once) this rank's gathered buffer for `world` ranks. */
+SA_API sa_status sa_ctx_gather_buffer(sa_ctx* ctx, int32_t world, void** buf_out,
+                                      size_t* bytes_out);
+/* peer_bufs: host array [world] of device pointers, peer_bufs[rank] = own. */
+SA_API sa_status sa_ctx_gather_attach(sa_ctx* ctx, int32_t rank, void* const* peer_bufs);
+/* Enqueue the wait for the latest attention's outputs from every rank;
+ * *gathered_out (nullable) = the slot holding them [seqs][layers][world*QH][D].
+ * A wait that gives up sets SA_DEV_TIMEOUT in the status word. */
+SA_API sa_status sa_ctx_gather_wait(sa_ctx* ctx, void** gathered_out);
+/* CUDA IPC handle of a device allocation (SA_IPC_HANDLE_BYTES bytes), and
+ * mapping / unmapping another process's allocation on `device`. */
+SA_API sa_status sa_ipc_export(int32_t device, const void* dev_ptr, void* handle_out);
+SA_API sa_status sa_ipc_open(int32_t device, const void* handle, void** dev_ptr_out);
+SA_API sa_status sa_ipc_close(int32_t device, void* dev_ptr);
+
 #ifdef __cplusplus
 }
 #endif

@@ -375,7 +375,58 @@ class DecodeContext:
     def launches(self) -> int:
         return int(self._lib.sa_ctx_launch_count(self._h))
 
+    # ---- KV-head sharding: outputs gathered over peer memory
+    def gather_buffer(self, world: int) -> tuple[int, int]:
+        """(device pointer, bytes) of this rank's gathered buffer for `world` ranks."""
+        ptr, nbytes = C.c_void_p(), C.c_size_t()
+        check(self._lib.sa_ctx_gather_buffer(self._h, world, C.byref(ptr), C.byref(nbytes)),
+              "sa_ctx_gather_buffer")
+        self._gather_world = world
+        return int(ptr.value), int(nbytes.value)
+
+    def gather_attach(self, rank: int, peer_ptrs) -> None:
+        """Attach every rank's gathered buffer (device pointers, own at `rank`)."""
+        arr = (C.c_void_p * len(peer_ptrs))(*[int(x) for x in peer_ptrs])
+        check(self._lib.sa_ctx_gather_attach(self._h, rank, arr), "sa_ctx_gather_attach")
+
+    def enable_gather(self, world: int, rank: int, group=None) -> None:
+        """Exchange gathered-buffer IPC handles with the other ranks of a
+        torch.distributed group and attach them (one process per GPU)."""
+        import torch.distributed as dist
+
+        own, _ = self.gather_buffer(world)
+        handle = (C.c_uint8 * 64)()
+        check(self._lib.sa_ipc_export(self.device.index, C.c_void_p(own), handle), "sa_ipc_export")
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._opened = []
+        ptrs = []
+        for r, h in enumerate(handles):
+            if r == rank:
+                ptrs.append(own)
+                continue
+            buf = (C.c_uint8 * 64).from_buffer_copy(h)
+            ptr = C.c_void_p()
+            check(self._lib.sa_ipc_open(self.device.index, buf, C.byref(ptr)), "sa_ipc_open")
+            self._opened.append(int(ptr.value))
+            ptrs.append(int(ptr.value))
+        self.gather_attach(rank, ptrs)
+
+    def gather_wait(self, view: bool = True) -> torch.Tensor | None:
+        """Enqueue the wait for every rank's outputs of the latest attention;
+        returns the gathered slot [S, L, world*QH, 128] (valid until the
+        attention after next), or None when view is False."""
+        ptr = C.c_void_p()
+        check(self._lib.sa_ctx_gather_wait(self._h, C.byref(ptr)), "sa_ctx_gather_wait")
+        if not view:
+            return None
+        return _view(int(ptr.value), (self.seqs, self.layers, self._gather_world * self.qh, HEAD_DIM),
+                     torch.float16 if self.out_fp16 else torch.float32, self.device)
+
     def close(self) -> None:
+        for ptr in getattr(self, "_opened", []):
+            self._lib.sa_ipc_close(self.device.index, C.c_void_p(ptr))
+        self._opened = []
         if getattr(self, "_h", None):
             self._lib.sa_ctx_destroy(self._h)
             self._h = None

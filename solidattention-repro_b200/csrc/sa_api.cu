@@ -145,6 +145,13 @@ struct sa_ctx {
   uint32_t* h_status = nullptr;  // pinned
   std::vector<uint8_t> prefilled;
   uint64_t launches = 0;
+  // KV-head-sharded gather over peer memory: two parity slots of
+  // [seqs*layers][world * QH][D] outputs, then a 64-bit arrival counter
+  uint8_t* gather_buf = nullptr;
+  size_t gather_slot_bytes = 0, gather_counter_bytes = 0, gather_bytes = 0;
+  int gather_world = 0, gather_rank = -1;
+  void** gather_peers = nullptr;  // device array [gather_world]
+  uint64_t gather_attends = 0;
 };
 
 extern "C" {
@@ -673,8 +680,17 @@ sa_status ctx_attend(sa_ctx* c, const float* query, void* out) {
   p.partial = c->attn_partial;
   p.counters = c->attn_counters;
   p.status = c->dev.status;
+  if (c->gather_peers) {
+    p.gather_peers = c->gather_peers;
+    p.gather_world = c->gather_world;
+    p.gather_rank = c->gather_rank;
+    p.gather_slot_bytes = (size_t)(c->gather_attends % 2) * c->gather_slot_bytes;
+    p.gather_counter_bytes = c->gather_counter_bytes;
+  }
   ++c->launches;
-  return launch_attention(p, c->pool_map, c->stream);
+  const sa_status st = launch_attention(p, c->pool_map, c->stream);
+  if (st == SA_OK && c->gather_peers) ++c->gather_attends;
+  return st;
 }
 
 }  // namespace
@@ -772,7 +788,8 @@ SA_API sa_status sa_ctx_destroy(sa_ctx* c) {
   void* ptrs[] = {d.pool, d.reps, d.table, d.num_sealed, d.tail_block, d.tail_len, d.generation,
                   d.query_ring, d.free_list, d.free_top, d.seal_counters, d.status, c->selected,
                   c->selected_count, c->scores, c->select_counters, c->attn_partial,
-                  c->attn_counters, c->d_query, c->d_kv_new, c->d_out};
+                  c->attn_counters, c->d_query, c->d_kv_new, c->d_out, c->gather_buf,
+                  c->gather_peers};
   for (void* p : ptrs) cudaFree(p);
   if (c->h_status) cudaFreeHost(c->h_status);
   if (c->own_stream && c->stream) cudaStreamDestroy(c->stream);
@@ -977,5 +994,96 @@ SA_API sa_status sa_ctx_sync(sa_ctx* c, uint32_t* bits_out) {
 }
 
 SA_API uint64_t sa_ctx_launch_count(const sa_ctx* c) { return c ? c->launches : 0; }
+
+// ------------------------------------------- KV-head-sharded gather over peer memory
+
+SA_API sa_status sa_ctx_gather_buffer(sa_ctx* c, int32_t world, void** buf_out,
+                                      size_t* bytes_out) {
+  if (!c || !buf_out || world < 1 || world > 64)
+    return fail(SA_ERR_INVALID_ARG, "gather_buffer: bad argument");
+  if (c->gather_buf && c->gather_world != world)
+    return fail(SA_ERR_INVALID_ARG, "gather_buffer: already allocated for another world size");
+  DeviceGuard guard(c->cfg.device);
+  if (!c->gather_buf) {
+    const size_t esz = c->cfg.out_fp16 ? 2 : 4;
+    const size_t slot = (size_t)c->num_sl * world * c->cfg.query_heads * kHeadDim * esz;
+    c->gather_slot_bytes = (slot + 255) & ~size_t(255);
+    c->gather_counter_bytes = 2 * c->gather_slot_bytes;
+    c->gather_bytes = c->gather_counter_bytes + 256;
+    sa_status st = dalloc(&c->gather_buf, c->gather_bytes);
+    if (st != SA_OK) return st;
+    SA_CUDA_TRY(cudaMemset(c->gather_buf, 0, c->gather_bytes));
+    c->gather_world = world;
+  }
+  *buf_out = c->gather_buf;
+  if (bytes_out) *bytes_out = c->gather_bytes;
+  return SA_OK;
+}
+
+SA_API sa_status sa_ctx_gather_attach(sa_ctx* c, int32_t rank, void* const* peer_bufs) {
+  if (!c || !peer_bufs) return fail(SA_ERR_INVALID_ARG, "gather_attach: null argument");
+  if (!c->gather_buf) return fail(SA_ERR_INVALID_ARG, "gather_attach: call sa_ctx_gather_buffer first");
+  if (rank < 0 || rank >= c->gather_world)
+    return fail(SA_ERR_INVALID_ARG, "gather_attach: rank outside [0, world)");
+  if (peer_bufs[rank] != c->gather_buf)
+    return fail(SA_ERR_INVALID_ARG, "gather_attach: peer_bufs[rank] must be this context's buffer");
+  for (int r = 0; r < c->gather_world; ++r)
+    if (!peer_bufs[r] || (reinterpret_cast<uintptr_t>(peer_bufs[r]) & 255u))
+      return fail(SA_ERR_INVALID_ARG, "gather_attach: null or unaligned peer buffer");
+  DeviceGuard guard(c->cfg.device);
+  if (!c->gather_peers) {
+    sa_status st = dalloc(&c->gather_peers, (size_t)c->gather_world);
+    if (st != SA_OK) return st;
+  }
+  SA_CUDA_TRY(cudaMemcpy(c->gather_peers, peer_bufs, sizeof(void*) * c->gather_world,
+                         cudaMemcpyHostToDevice));
+  c->gather_rank = rank;
+  return SA_OK;
+}
+
+SA_API sa_status sa_ctx_gather_wait(sa_ctx* c, void** gathered_out) {
+  if (!c) return fail(SA_ERR_INVALID_ARG, "gather_wait: null ctx");
+  if (!c->gather_peers) return fail(SA_ERR_INVALID_ARG, "gather_wait: gather not attached");
+  if (c->gather_attends == 0) return fail(SA_ERR_INVALID_ARG, "gather_wait: no gathered attend yet");
+  DeviceGuard guard(c->cfg.device);
+  const unsigned long long units = (unsigned long long)c->num_sl * c->cfg.kv_heads;
+  const unsigned long long expected = c->gather_attends * c->gather_world * units;
+  ++c->launches;
+  const sa_status st = launch_gather_wait(
+      reinterpret_cast<const unsigned long long*>(c->gather_buf + c->gather_counter_bytes),
+      expected, c->dev.status, c->stream);
+  if (st != SA_OK) return st;
+  if (gathered_out)
+    *gathered_out = c->gather_buf + ((c->gather_attends - 1) % 2) * c->gather_slot_bytes;
+  return SA_OK;
+}
+
+SA_API sa_status sa_ipc_export(int32_t device, const void* dev_ptr, void* handle_out) {
+  if (!dev_ptr || !handle_out) return fail(SA_ERR_INVALID_ARG, "ipc_export: null argument");
+  DeviceGuard guard(device);
+  if (!guard.ok()) return fail(SA_ERR_CUDA, "ipc_export: cudaSetDevice failed");
+  cudaIpcMemHandle_t h;
+  SA_CUDA_TRY(cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr)));
+  static_assert(sizeof(h) == SA_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle_out, &h, sizeof(h));
+  return SA_OK;
+}
+
+SA_API sa_status sa_ipc_open(int32_t device, const void* handle, void** dev_ptr_out) {
+  if (!handle || !dev_ptr_out) return fail(SA_ERR_INVALID_ARG, "ipc_open: null argument");
+  DeviceGuard guard(device);
+  if (!guard.ok()) return fail(SA_ERR_CUDA, "ipc_open: cudaSetDevice failed");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  SA_CUDA_TRY(cudaIpcOpenMemHandle(dev_ptr_out, h, cudaIpcMemLazyEnablePeerAccess));
+  return SA_OK;
+}
+
+SA_API sa_status sa_ipc_close(int32_t device, void* dev_ptr) {
+  if (!dev_ptr) return SA_OK;
+  DeviceGuard guard(device);
+  SA_CUDA_TRY(cudaIpcCloseMemHandle(dev_ptr));
+  return SA_OK;
+}
 
 }  // extern "C"

@@ -95,6 +95,7 @@ struct alignas(128) AttnSmem {
   int seg_unit[kMaxSegments];
   int seg_index[kMaxSegments];       // the CTA's place among its unit's CTAs
   int seg_count[kMaxSegments];       // CTAs covering the unit
+  alignas(16) uint8_t ostage[G * kHeadDim * 4];  // a unit's output, for peer stores
   uint64_t full[kStages];
   int released[kStages];      // warps done with the stage's current contents
   int stage_issues[kStages];  // loads issued into the stage so far
@@ -219,9 +220,49 @@ __device__ __forceinline__ void issue_stage(AttnSmem<G>& s, const CUtensorMap* m
   s.stage_issues[stage] += 1;
 }
 
-__device__ __forceinline__ void store_out(const AttnParams& p, size_t idx, float v) {
-  if (p.out_fp16) reinterpret_cast<uint16_t*>(p.out)[idx] = f2h_rn(v);
-  else reinterpret_cast<float*>(p.out)[idx] = v;
+// Stores output element idx of unit u (local layout) and, when gathering,
+// stages it for the peer stores.
+template <int G>
+__device__ __forceinline__ void store_out(const AttnParams& p, AttnSmem<G>& s, size_t base,
+                                          int idx, float v) {
+  if (p.out_fp16) {
+    const uint16_t h = f2h_rn(v);
+    reinterpret_cast<uint16_t*>(p.out)[base + idx] = h;
+    if (p.gather_peers) reinterpret_cast<uint16_t*>(s.ostage)[idx] = h;
+  } else {
+    reinterpret_cast<float*>(p.out)[base + idx] = v;
+    if (p.gather_peers) reinterpret_cast<float*>(s.ostage)[idx] = v;
+  }
+}
+
+// Copies unit u's staged output into every rank's gathered buffer (16-byte
+// P2P stores over NVLink; the own rank's buffer is local), then counts one
+// arrival on every rank's counter. The barrier orders all threads' stores
+// before thread 0's system-scope fence and atomics.
+template <int G>
+__device__ __forceinline__ void gather_push(const AttnParams& p, AttnSmem<G>& s, int u) {
+  __syncthreads();
+  const int esz = p.out_fp16 ? 2 : 4;
+  const int chunks = G * kHeadDim * esz / 16;
+  const int sl = u / p.kv_heads;
+  const int kvh = u - sl * p.kv_heads;
+  const size_t off = p.gather_slot_bytes +
+                     (((size_t)sl * p.gather_world + p.gather_rank) * p.kv_heads + kvh) *
+                         (size_t)(G * kHeadDim * esz);
+  for (int i = threadIdx.x; i < chunks * p.gather_world; i += kThreads) {
+    const int r = i / chunks;
+    const int c = i - r * chunks;
+    uint8_t* dst = reinterpret_cast<uint8_t*>(p.gather_peers[r]) + off + (size_t)c * 16;
+    *reinterpret_cast<uint4*>(dst) = reinterpret_cast<const uint4*>(s.ostage)[c];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int r = 0; r < p.gather_world; ++r)
+      atomicAdd_system(reinterpret_cast<unsigned long long*>(
+                           reinterpret_cast<uint8_t*>(p.gather_peers[r]) + p.gather_counter_bytes),
+                       1ull);
+  }
 }
 
 // acc[g] += p(token, g) * v(token) over the half-warp's 4 tokens; tokens at
@@ -519,8 +560,9 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
           for (int w = 0; w < kConsumerWarps; ++w)
             o += accw[(w * G + g) * kHeadDim + d] * s.wscale[w][g];
           const float L = s.cta_l[g];
-          store_out(p, out_base + idx, L > 0.f ? o / L : 0.f);
+          store_out<G>(p, s, out_base, idx, L > 0.f ? o / L : 0.f);
         }
+        if (p.gather_peers) gather_push<G>(p, s, u);
       } else {
         float* part =
             p.partial + ((size_t)u * p.max_segments + s.seg_index[seg]) * G * kPartialStride;
@@ -560,9 +602,10 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
                 o += __ldcg(pk + 2 + d) * f;
               }
             }
-            store_out(p, out_base + idx, L > 0.f ? o / L : 0.f);
+            store_out<G>(p, s, out_base, idx, L > 0.f ? o / L : 0.f);
           }
           if (threadIdx.x == 0) p.counters[u] = 0;
+          if (p.gather_peers) gather_push<G>(p, s, u);
         }
       }
       __syncthreads();  // the stage buffer is free again
@@ -611,7 +654,29 @@ sa_status launch_g(const AttnParams& p, const CUtensorMap& map, cudaStream_t str
                       : launch_layout<G, false>(p, map, stream);
 }
 
+__global__ void gather_wait_kernel(const unsigned long long* counter, unsigned long long expected,
+                                   uint32_t* status) {
+  if (threadIdx.x != 0) return;
+  const long long start = clock64();
+  for (;;) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(counter) : "memory");
+    if (v >= expected) break;
+    if (clock64() - start > kWaitLimitCycles) {
+      raise_status(status, SA_DEV_TIMEOUT);
+      break;
+    }
+    __nanosleep(256);
+  }
+}
+
 }  // namespace
+
+sa_status launch_gather_wait(const unsigned long long* counter, unsigned long long expected,
+                             uint32_t* status, cudaStream_t stream) {
+  gather_wait_kernel<<<1, 32, 0, stream>>>(counter, expected, status);
+  return cuda_status(cudaGetLastError(), "gather_wait_kernel launch");
+}
 
 AttnPlan attention_plan(int units, int slots_per_unit, int group) {
   const long long E = std::max(1, slots_per_unit);

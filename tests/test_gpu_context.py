@@ -258,3 +258,47 @@ def test_kv_head_shards_reassemble_the_unsharded_step(pkg, cuda):
         assert ctx.status_bits() == 0
         ctx.close()
     full.close()
+
+
+def test_gather_over_peer_buffers_assembles_all_heads(pkg, cuda):
+    """The attention epilogue's gather: two KV-head shards of one sequence
+    (emulated ranks on one GPU, one stream, so every wait is satisfied when it
+    runs) store their outputs into both ranks' gathered buffers; each buffer's
+    slot then holds the full head set, equal to the unsharded context's output,
+    for consecutive steps (alternating slots)."""
+    import dataclasses
+
+    from solidattention_repro_b200 import sharding, workloads
+
+    w = dataclasses.replace(workloads.CONFIGS["cfg3"], name="gather-test", layers=3,
+                            context_blocks=80, budget_blocks=16, hot_blocks=4)
+    full, info = workloads.make_context(w, 8, cuda, seed=4)
+    q, kv = workloads.decode_inputs(w, info, 3, cuda, seed=4)
+    ranks = []
+    for r in range(2):
+        sl = sharding.shard_kv_heads(w.kv_heads, 2, r)
+        ctx, inf = workloads.make_context(w, 8, cuda, seed=4, kv_heads_slice=sl)
+        qs, kvs = workloads.decode_inputs(w, inf, 3, cuda, seed=4, kv_heads_slice=sl)
+        ranks.append((ctx, qs, kvs))
+    bufs = [ctx.gather_buffer(2)[0] for ctx, _, _ in ranks]
+    for r, (ctx, _, _) in enumerate(ranks):
+        ctx.gather_attach(r, bufs)
+    with pytest.raises(pkg.SparseKVError):
+        ranks[0][0].gather_wait()  # nothing gathered yet
+    slots = set()
+    for step in range(3):
+        want = full.step(q[step], kv[step]).float().cpu().numpy()
+        locals_ = [ctx.step(qs[step], kvs[step]).float().cpu().numpy() for ctx, qs, kvs in ranks]
+        for r, (ctx, _, _) in enumerate(ranks):
+            got_t = ctx.gather_wait()
+            ctx.sync()
+            slots.add(got_t.data_ptr() - bufs[r])
+            got = got_t.float().cpu().numpy()
+            assert np.array_equal(got, sharding.assemble_heads(locals_, w.group)), (step, r)
+            assert np.abs(got - want).max() <= 2e-3 and \
+                cosine(got.ravel(), want.ravel()) >= 0.999999, (step, r)
+    assert len(slots) == 2  # consecutive attends alternate between the two slots
+    for ctx, _, _ in ranks:
+        assert ctx.status_bits() == 0
+        ctx.close()
+    full.close()
