@@ -624,7 +624,9 @@ sa_status dalloc(T** p, size_t count) {
   return SA_OK;
 }
 
-sa_status ctx_select(sa_ctx* c, const float* query) {
+// kv_new non-null: the select kernel also appends the step's token (fused).
+sa_status ctx_select(sa_ctx* c, const float* query, const void* kv_new = nullptr,
+                     int kv_fp32 = 0) {
   SelectParams p{};
   p.query = query;
   p.reps = c->dev.reps;
@@ -648,12 +650,19 @@ sa_status ctx_select(sa_ctx* c, const float* query) {
   p.scores = c->scores;
   p.counters = c->select_counters;
   p.status = c->dev.status;
+  if (kv_new) {
+    p.append_ctx = c->dev;
+    p.append_kv = kv_new;
+    p.append_kv_fp32 = kv_fp32;
+  }
   ++c->launches;
   return launch_select(p, c->stream);
 }
 
-sa_status ctx_attend(sa_ctx* c, const float* query, void* out) {
+// pending: tokens appended by a fused append this step, not yet in tail_len.
+sa_status ctx_attend(sa_ctx* c, const float* query, void* out, int pending = 0) {
   AttnParams p{};
+  p.tail_pending = pending;
   p.pool = c->dev.pool;
   p.head_major = 1;
   p.kv_heads = c->cfg.kv_heads;
@@ -941,21 +950,23 @@ SA_API sa_status sa_ctx_attend(sa_ctx* c, const float* query, void* out) {
 SA_API sa_status sa_ctx_seal(sa_ctx* c) {
   if (!c) return fail(SA_ERR_INVALID_ARG, "seal: null ctx");
   DeviceGuard guard(c->cfg.device);
-  c->launches += 2;
-  return launch_seal(c->dev, c->stream);
+  ++c->launches;
+  return launch_seal(c->dev, 0, c->stream);
 }
 
 SA_API sa_status sa_ctx_step(sa_ctx* c, const float* query, const void* kv_new, int32_t kv_fp32,
                              void* out) {
   if (!c || !query || !kv_new || !out) return fail(SA_ERR_INVALID_ARG, "step: null argument");
   DeviceGuard guard(c->cfg.device);
+  // Three launches: select with the fused append (the new token is written
+  // but not yet counted in tail_len), attention counting that pending token,
+  // then the seal kernel, which rebuilds full tails and stores every tail's
+  // new length.
   sa_status st;
+  if ((st = ctx_select(c, query, kv_new, kv_fp32)) != SA_OK) return st;
+  if ((st = ctx_attend(c, query, out, 1)) != SA_OK) return st;
   ++c->launches;
-  if ((st = launch_append(c->dev, query, kv_new, kv_fp32, c->stream)) != SA_OK) return st;
-  if ((st = ctx_select(c, query)) != SA_OK) return st;
-  if ((st = ctx_attend(c, query, out)) != SA_OK) return st;
-  c->launches += 2;
-  return launch_seal(c->dev, c->stream);
+  return launch_seal(c->dev, 1, c->stream);
 }
 
 SA_API sa_status sa_ctx_step_host(sa_ctx* c, const float* query_host, const void* kv_new_host,

@@ -350,6 +350,7 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
     int nsel = p.sel_count ? p.sel_count[sl * p.n_sel_groups + sgroup] : p.fixed_nsel;
     nsel = max(0, min(nsel, p.sel_ids ? p.sel_stride : nsel));
     int tail_len = p.tail_len ? p.tail_len[sl] : p.fixed_tail_len;
+    if (tail_len < kBlockTokens) tail_len += p.tail_pending;
     tail_len = max(0, min(tail_len, kBlockTokens));
     int phys, ntok;
     unit_entry(p, sl, sgroup, nsel, tail_len, e, &phys, &ntok);

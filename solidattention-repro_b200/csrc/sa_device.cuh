@@ -164,4 +164,61 @@ __device__ __forceinline__ int block_exclusive_scan(int value, int* scratch, int
   return before;
 }
 
+// ---- decode-tail append ------------------------------------------------------
+
+// Writes the step's K/V of KV heads [kvh0, kvh1) of sequence-layer sl into
+// row tail_len[sl] of its head-major tail block (plane (h, kv) row tl) and
+// the queries of query heads [qh0, qh1) into the tail's query ring. tail_len
+// is not changed. kv_new rows are [num_sl][2][kv_heads][128], FP16 or FP32
+// (packed to FP16 with round-to-nearest-even). Every thread of the CTA calls
+// it (index tid of nthreads); false, with a status bit, when the tail is
+// full or its block id is invalid (the decision is uniform over the CTA).
+__device__ __forceinline__ bool append_token(const CtxDev& c, int sl, const float* query,
+                                             const void* kv_new, int kv_fp32, int kvh0, int kvh1,
+                                             int qh0, int qh1, int tid, int nthreads) {
+  const int tl = c.tail_len[sl];
+  const int phys = c.tail_block[sl];
+  if (tl < 0 || tl >= kBlockTokens) {
+    if (tid == 0) raise_status(c.status, SA_DEV_TAIL_FULL);
+    return false;
+  }
+  if (phys < 0 || phys >= c.pool_blocks) {
+    if (tid == 0) raise_status(c.status, SA_DEV_BAD_BLOCK);
+    return false;
+  }
+  uint16_t* block = c.pool + (int64_t)phys * c.kv_heads * 2 * kBlockTokens * kHeadDim;
+  constexpr int kChunksPerPlane = kHeadDim / 8;  // 16-byte FP16 chunks of one head row
+  const int heads = kvh1 - kvh0;
+  const int chunks = 2 * heads * kChunksPerPlane;
+  for (int i = tid; i < chunks; i += nthreads) {
+    const int kv = i / (heads * kChunksPerPlane);
+    const int rem = i - kv * heads * kChunksPerPlane;
+    const int h = kvh0 + rem / kChunksPerPlane;
+    const int d = (rem % kChunksPerPlane) * 8;
+    const int64_t src = (((int64_t)sl * 2 + kv) * c.kv_heads + h) * kHeadDim + d;
+    uint4* dst = reinterpret_cast<uint4*>(block + (((int64_t)h * 2 + kv) * kBlockTokens + tl) *
+                                                      kHeadDim + d);
+    if (kv_fp32) {
+      const float4* f = reinterpret_cast<const float4*>(static_cast<const float*>(kv_new) + src);
+      const float4 a = f[0], b = f[1];
+      *dst = make_uint4((uint32_t)f2h_rn(a.x) | ((uint32_t)f2h_rn(a.y) << 16),
+                        (uint32_t)f2h_rn(a.z) | ((uint32_t)f2h_rn(a.w) << 16),
+                        (uint32_t)f2h_rn(b.x) | ((uint32_t)f2h_rn(b.y) << 16),
+                        (uint32_t)f2h_rn(b.z) | ((uint32_t)f2h_rn(b.w) << 16));
+    } else {
+      *dst = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(kv_new) + src);
+    }
+  }
+  float* ring = c.query_ring + (int64_t)sl * c.qh * kBlockTokens * kHeadDim;
+  const float* q = query + (int64_t)sl * c.qh * kHeadDim;
+  const int qchunks = (qh1 - qh0) * kHeadDim / 4;
+  for (int i = tid; i < qchunks; i += nthreads) {
+    const int h = qh0 + (4 * i) / kHeadDim;
+    const int d = (4 * i) % kHeadDim;
+    *reinterpret_cast<float4*>(ring + ((int64_t)h * kBlockTokens + tl) * kHeadDim + d) =
+        *reinterpret_cast<const float4*>(q + (int64_t)h * kHeadDim + d);
+  }
+  return true;
+}
+
 }  // namespace sa

@@ -38,6 +38,30 @@ constexpr int kMaxDevices = 64;
 sa_status make_row_tensor_map(CUtensorMap* map, const void* base, uint64_t row_elems,
                               uint64_t rows);
 
+// ---- decode-context device state (owned by sa_api.cu) -------------------------
+
+struct CtxDev {
+  uint16_t* pool;      // head-major: [pool_blocks][kv_heads][K,V][32][128]
+  int64_t row_elems;   // 2 * kv_heads * 128 (one token of every head)
+  int pool_blocks;
+  float* reps;         // [num_sl][qh][128][reps_cap]
+  int reps_cap;        // table_blocks rounded up to a multiple of 4
+  int32_t* table;      // [num_sl][table_blocks]
+  int table_blocks;
+  int32_t* num_sealed;
+  int32_t* tail_block;
+  int32_t* tail_len;
+  int32_t* generation;
+  float* query_ring;   // [num_sl][qh][32][128]
+  int32_t* free_list;
+  int32_t* free_top;
+  int* seal_counters;  // [1] arrivals of the seal kernel's CTAs
+  uint32_t* status;
+  int num_sl, qh, kv_heads;
+  int rep_window, rep_topk;
+  float rep_scale;
+};
+
 // ---- attention (sa_attention.cu) -----------------------------------------------
 
 struct AttnParams {
@@ -62,6 +86,7 @@ struct AttnParams {
   const int32_t* tail_len;    // null -> fixed_tail_len
   int fixed_tail_block;
   int fixed_tail_len;
+  int tail_pending;    // tokens appended this step but not yet counted in tail_len
   const float* query;  // [num_sl][kv_heads*group][128]
   void* out;           // [num_sl][kv_heads*group][128]
   int out_fp16;
@@ -117,6 +142,14 @@ struct SelectParams {
   float* scores;      // [num_sl][n_groups][nb_cap]
   int* counters;      // [num_sl][n_groups], zero between launches
   uint32_t* status;
+  // Fused append (append_kv null = off): the first CTA of each unit writes
+  // the step's K/V of the group's KV heads into row tail_len of the
+  // sequence-layer's tail block and the group's queries into the query ring.
+  // tail_len itself is left unchanged: the step's attention and seal count
+  // the pending token (several units share one sequence-layer's tail).
+  CtxDev append_ctx;
+  const void* append_kv;  // [num_sl][2][kv_heads][128] FP16, or FP32 when append_kv_fp32
+  int append_kv_fp32;
 };
 
 int select_max_blocks();
@@ -152,31 +185,13 @@ sa_status launch_build_reps(const RepParams& p, cudaStream_t stream);
 // (queries q + (h * blocks * 32 + b * 32 + p) * d, i.e. [qh][blocks*32][d]).
 sa_status launch_build_reps_per_block(const RepParams& p, cudaStream_t stream);
 
-struct CtxDev {
-  uint16_t* pool;      // head-major: [pool_blocks][kv_heads][K,V][32][128]
-  int64_t row_elems;   // 2 * kv_heads * 128 (one token of every head)
-  int pool_blocks;
-  float* reps;         // [num_sl][qh][128][reps_cap]
-  int reps_cap;        // table_blocks rounded up to a multiple of 4
-  int32_t* table;      // [num_sl][table_blocks]
-  int table_blocks;
-  int32_t* num_sealed;
-  int32_t* tail_block;
-  int32_t* tail_len;
-  int32_t* generation;
-  float* query_ring;   // [num_sl][qh][32][128]
-  int32_t* free_list;
-  int32_t* free_top;
-  int* seal_counters;  // [num_sl]
-  uint32_t* status;
-  int num_sl, qh, kv_heads;
-  int rep_window, rep_topk;
-  float rep_scale;
-};
 
 sa_status launch_append(const CtxDev& c, const float* query, const void* kv_new, int kv_fp32,
                         cudaStream_t stream);
-sa_status launch_seal(const CtxDev& c, cudaStream_t stream);
+// Rebuild the representative of every full tail and commit the seals.
+// pending = tokens appended by a fused append and not yet in tail_len (the
+// commit then stores every tail's new length).
+sa_status launch_seal(const CtxDev& c, int pending, cudaStream_t stream);
 sa_status launch_pack_kv(uint16_t* packed, const float* key, const float* value,
                          size_t token, size_t elements, cudaStream_t stream);
 sa_status launch_xor(const uint8_t* in, uint8_t* out, size_t bytes, uint8_t mask,

@@ -206,42 +206,48 @@ __global__ void __launch_bounds__(kRepThreads) reps_kernel(const RepParams p, in
   rep_block(c, rep_smem());
 }
 
-// grid (qh, num_sl): rebuild the representative of every full tail.
-__global__ void __launch_bounds__(kRepThreads) seal_rebuild_kernel(const CtxDev c) {
-  const int h = blockIdx.x, sl = blockIdx.y;
-  if (c.tail_len[sl] >= kBlockTokens && c.num_sealed[sl] < c.table_blocks) {
-    const int nb = c.num_sealed[sl];
-    const int phys = c.tail_block[sl];
-    if (phys >= 0 && phys < c.pool_blocks) {
-      RepCall r;
-      r.q = c.query_ring + ((int64_t)sl * c.qh + h) * kBlockTokens * kHeadDim;
-      r.tokens = kBlockTokens;
-      r.block = 0;
-      r.kv = c.pool;
-      r.head_major = 1;
-      r.kv_heads = c.kv_heads;
-      r.row_stride = c.row_elems;
-      r.kv_head = h / (c.qh / c.kv_heads);
-      r.d = kHeadDim;
-      r.table = nullptr;
-      r.table_base = 0;
-      r.row_base = (int64_t)phys * kBlockTokens;
-      r.pool_rows = (int64_t)c.pool_blocks * kBlockTokens;
-      r.window = c.rep_window;
-      r.topk = c.rep_topk;
-      r.scale = c.rep_scale;
-      r.out_values = c.reps + ((int64_t)sl * c.qh + h) * kHeadDim * c.reps_cap + nb;
-      r.o_dim = c.reps_cap;
-      r.out_offsets = nullptr;
-      r.status = c.status;
-      rep_block(r, rep_smem());
-    }
-  }
+// Tail length of sequence-layer sl once the step's pending tokens count (a
+// tail that was already full received no append).
+__device__ __forceinline__ int effective_tail(const CtxDev& c, int sl, int pending) {
+  const int tl = c.tail_len[sl];
+  return tl < kBlockTokens ? tl + pending : tl;
+}
+
+// Rebuild the representative of query head h of sequence-layer sl if its
+// tail is full.
+__device__ void seal_rebuild(const CtxDev& c, int h, int sl, int pending) {
+  if (effective_tail(c, sl, pending) < kBlockTokens || c.num_sealed[sl] >= c.table_blocks) return;
+  const int nb = c.num_sealed[sl];
+  const int phys = c.tail_block[sl];
+  if (phys < 0 || phys >= c.pool_blocks) return;
+  RepCall r;
+  r.q = c.query_ring + ((int64_t)sl * c.qh + h) * kBlockTokens * kHeadDim;
+  r.tokens = kBlockTokens;
+  r.block = 0;
+  r.kv = c.pool;
+  r.head_major = 1;
+  r.kv_heads = c.kv_heads;
+  r.row_stride = c.row_elems;
+  r.kv_head = h / (c.qh / c.kv_heads);
+  r.d = kHeadDim;
+  r.table = nullptr;
+  r.table_base = 0;
+  r.row_base = (int64_t)phys * kBlockTokens;
+  r.pool_rows = (int64_t)c.pool_blocks * kBlockTokens;
+  r.window = c.rep_window;
+  r.topk = c.rep_topk;
+  r.scale = c.rep_scale;
+  r.out_values = c.reps + ((int64_t)sl * c.qh + h) * kHeadDim * c.reps_cap + nb;
+  r.o_dim = c.reps_cap;
+  r.out_offsets = nullptr;
+  r.status = c.status;
+  rep_block(r, rep_smem());
 }
 
 // One CTA: commit every full tail in (sequence-layer) order, so the physical
-// block each new tail receives is deterministic.
-__global__ void __launch_bounds__(256) seal_commit_kernel(const CtxDev c) {
+// block each new tail receives is deterministic; with pending tokens, store
+// every other tail's new length.
+__device__ void seal_commit(const CtxDev& c, int pending) {
   __shared__ int scan[33];
   __shared__ int base_top;
   if (threadIdx.x == 0) base_top = *c.free_top;
@@ -250,11 +256,15 @@ __global__ void __launch_bounds__(256) seal_commit_kernel(const CtxDev c) {
   for (int sl0 = 0; sl0 < c.num_sl; sl0 += blockDim.x) {
     const int sl = sl0 + threadIdx.x;
     int want = 0;
-    if (sl < c.num_sl && c.tail_len[sl] >= kBlockTokens) {
-      if (c.num_sealed[sl] >= c.table_blocks) raise_status(c.status, SA_DEV_TABLE_FULL);
-      else if (c.tail_block[sl] < 0 || c.tail_block[sl] >= c.pool_blocks)
-        raise_status(c.status, SA_DEV_BAD_BLOCK);
-      else want = 1;
+    int len = 0;
+    if (sl < c.num_sl) {
+      len = effective_tail(c, sl, pending);
+      if (len >= kBlockTokens) {
+        if (c.num_sealed[sl] >= c.table_blocks) raise_status(c.status, SA_DEV_TABLE_FULL);
+        else if (c.tail_block[sl] < 0 || c.tail_block[sl] >= c.pool_blocks)
+          raise_status(c.status, SA_DEV_BAD_BLOCK);
+        else want = 1;
+      }
     }
     int total = 0;
     const int rank = taken_before + block_exclusive_scan(want, scan, &total);
@@ -262,6 +272,7 @@ __global__ void __launch_bounds__(256) seal_commit_kernel(const CtxDev c) {
       const int top = base_top - 1 - rank;
       if (top < 0) {
         raise_status(c.status, SA_DEV_POOL_EMPTY);
+        want = 0;
       } else {
         const int nb = c.num_sealed[sl];
         c.table[(int64_t)sl * c.table_blocks + nb] = c.tail_block[sl];
@@ -271,10 +282,35 @@ __global__ void __launch_bounds__(256) seal_commit_kernel(const CtxDev c) {
         c.generation[sl] += 1;
       }
     }
+    if (!want && pending && sl < c.num_sl) c.tail_len[sl] = len;
     taken_before += total;
   }
   __syncthreads();
   if (threadIdx.x == 0) *c.free_top = max(0, base_top - taken_before);
+}
+
+// Grid-stride over (query head, sequence-layer) items: rebuild the
+// representative of every full tail; the last CTA to finish commits the
+// seals (an atomic arrival count, reset by that CTA; no spinning).
+__global__ void __launch_bounds__(kRepThreads) seal_kernel(const CtxDev c, int pending) {
+  __shared__ int last;
+  const int items = c.qh * c.num_sl;
+  for (int i = blockIdx.x; i < items; i += gridDim.x) {
+    seal_rebuild(c, i % c.qh, i / c.qh, pending);
+    __syncthreads();  // the next item reuses the shared buffers
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // the barrier orders the CTA's representative stores before this fence
+    __threadfence();
+    last = atomicAdd(c.seal_counters, 1) == (int)gridDim.x - 1;
+    if (last) {
+      __threadfence();
+      *c.seal_counters = 0;
+    }
+  }
+  __syncthreads();
+  if (last) seal_commit(c, pending);
 }
 
 // grid num_sl: write the current token's K/V into its tail row (one row of
@@ -284,50 +320,9 @@ __global__ void __launch_bounds__(256)
     append_kernel(const CtxDev c, const float* query, const void* kv_new, int kv_fp32) {
   const int sl = blockIdx.x;
   const int tl = c.tail_len[sl];
-  const int phys = c.tail_block[sl];
-  if (tl < 0 || tl >= kBlockTokens) {
-    if (threadIdx.x == 0) raise_status(c.status, SA_DEV_TAIL_FULL);
+  if (!append_token(c, sl, query, kv_new, kv_fp32, 0, c.kv_heads, 0, c.qh, threadIdx.x,
+                    blockDim.x))
     return;
-  }
-  if (phys < 0 || phys >= c.pool_blocks) {
-    if (threadIdx.x == 0) raise_status(c.status, SA_DEV_BAD_BLOCK);
-    return;
-  }
-  // Input row [2 (K,V)][kv_heads][128]; plane (kv, h) lands at
-  // ((phys * kv_heads + h) * 2 + kv) * 32 + tl rows of 128 halves.
-  const int64_t n = c.row_elems;
-  uint16_t* block = c.pool + (int64_t)phys * c.kv_heads * 2 * kBlockTokens * kHeadDim;
-  if (kv_fp32) {
-    const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(kv_new) + sl * n);
-    for (int64_t i = threadIdx.x; i < n / 4; i += blockDim.x) {
-      const int64_t e = 4 * i;
-      const int kv = (int)(e / (c.kv_heads * kHeadDim));
-      const int h = (int)(e / kHeadDim) % c.kv_heads;
-      const int d = (int)(e % kHeadDim);
-      const float4 v = src[i];
-      const uint32_t lo = (uint32_t)f2h_rn(v.x) | ((uint32_t)f2h_rn(v.y) << 16);
-      const uint32_t hi = (uint32_t)f2h_rn(v.z) | ((uint32_t)f2h_rn(v.w) << 16);
-      *reinterpret_cast<uint2*>(block + (((int64_t)h * 2 + kv) * kBlockTokens + tl) * kHeadDim + d) =
-          make_uint2(lo, hi);
-    }
-  } else {
-    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(kv_new) + sl * n);
-    for (int64_t i = threadIdx.x; i < n / 8; i += blockDim.x) {
-      const int64_t e = 8 * i;
-      const int kv = (int)(e / (c.kv_heads * kHeadDim));
-      const int h = (int)(e / kHeadDim) % c.kv_heads;
-      const int d = (int)(e % kHeadDim);
-      *reinterpret_cast<uint4*>(block + (((int64_t)h * 2 + kv) * kBlockTokens + tl) * kHeadDim + d) =
-          src[i];
-    }
-  }
-  float* ring = c.query_ring + (int64_t)sl * c.qh * kBlockTokens * kHeadDim;
-  const float* q = query + (int64_t)sl * c.qh * kHeadDim;
-  for (int i = threadIdx.x; i < c.qh * kHeadDim / 4; i += blockDim.x) {
-    const int h = (4 * i) / kHeadDim, d = (4 * i) % kHeadDim;
-    *reinterpret_cast<float4*>(ring + ((int64_t)h * kBlockTokens + tl) * kHeadDim + d) =
-        reinterpret_cast<const float4*>(q)[i];
-  }
   __syncthreads();
   if (threadIdx.x == 0) c.tail_len[sl] = tl + 1;
 }
@@ -404,17 +399,16 @@ sa_status launch_append(const CtxDev& c, const float* query, const void* kv_new,
   return cuda_status(cudaGetLastError(), "append_kernel launch");
 }
 
-sa_status launch_seal(const CtxDev& c, cudaStream_t stream) {
+sa_status launch_seal(const CtxDev& c, int pending, cudaStream_t stream) {
   sa_status st = check_rep_params(kHeadDim, c.rep_window, c.rep_topk);
   if (st != SA_OK) return st;
-  if ((st = ensure_smem_limit((const void*)seal_rebuild_kernel, (int)sizeof(RepSmem), g_seal_smem)) !=
-      SA_OK)
+  if ((st = ensure_smem_limit((const void*)seal_kernel, (int)sizeof(RepSmem), g_seal_smem)) != SA_OK)
     return st;
-  if (c.num_sl > 65535) return fail(SA_ERR_UNSUPPORTED, "seal: more than 65535 sequence-layers");
-  seal_rebuild_kernel<<<dim3(c.qh, c.num_sl), kRepThreads, sizeof(RepSmem), stream>>>(c);
-  if ((st = cuda_status(cudaGetLastError(), "seal_rebuild_kernel launch")) != SA_OK) return st;
-  seal_commit_kernel<<<1, 256, 0, stream>>>(c);
-  return cuda_status(cudaGetLastError(), "seal_commit_kernel launch");
+  // two CTAs per SM at most: an idle step (no full tail) costs one short wave
+  const int items = c.qh * c.num_sl;
+  const int grid = std::max(1, std::min(items, 2 * 148));
+  seal_kernel<<<grid, kRepThreads, sizeof(RepSmem), stream>>>(c, pending);
+  return cuda_status(cudaGetLastError(), "seal_kernel launch");
 }
 
 sa_status launch_pack_kv(uint16_t* packed, const float* key, const float* value, size_t token,

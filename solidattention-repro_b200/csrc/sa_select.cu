@@ -120,6 +120,13 @@ __global__ void __launch_bounds__(kThreads)
   float* qs = smem;
   float* dots = smem + ((p.group * p.d + 3) & ~3);  // 16-byte aligned
 
+  if (p.append_kv && blockIdx.x == 0) {
+    // fused decode-tail append of this group's heads (tail_len unchanged)
+    const int q0 = g * p.group;
+    const int per_kv = p.qh / p.append_ctx.kv_heads;
+    append_token(p.append_ctx, sl, p.query, p.append_kv, p.append_kv_fp32, q0 / per_kv,
+                 (q0 + p.group) / per_kv, q0, q0 + p.group, threadIdx.x, kThreads);
+  }
   const float* qsrc = p.query + ((size_t)sl * p.qh + (size_t)g * p.group) * p.d;
   for (int i = threadIdx.x; i < p.group * p.d; i += kThreads) qs[i] = qsrc[i];
   __syncthreads();
