@@ -626,8 +626,9 @@ sa_status dalloc(T** p, size_t count) {
 
 // kv_new non-null: the select kernel also appends the step's token (fused).
 sa_status ctx_select(sa_ctx* c, const float* query, const void* kv_new = nullptr,
-                     int kv_fp32 = 0) {
+                     int kv_fp32 = 0, bool pdl = false) {
   SelectParams p{};
+  p.pdl = pdl;
   p.query = query;
   p.reps = c->dev.reps;
   p.s_dim = c->table_pad;
@@ -660,9 +661,11 @@ sa_status ctx_select(sa_ctx* c, const float* query, const void* kv_new = nullptr
 }
 
 // pending: tokens appended by a fused append this step, not yet in tail_len.
-sa_status ctx_attend(sa_ctx* c, const float* query, void* out, int pending = 0) {
+sa_status ctx_attend(sa_ctx* c, const float* query, void* out, int pending = 0,
+                     bool pdl = false) {
   AttnParams p{};
   p.tail_pending = pending;
+  p.pdl = pdl;
   p.pool = c->dev.pool;
   p.head_major = 1;
   p.kv_heads = c->cfg.kv_heads;
@@ -961,12 +964,16 @@ SA_API sa_status sa_ctx_step(sa_ctx* c, const float* query, const void* kv_new, 
   // Three launches: select with the fused append (the new token is written
   // but not yet counted in tail_len), attention counting that pending token,
   // then the seal kernel, which rebuilds full tails and stores every tail's
-  // new length.
+  // new length. Attention and seal are programmatic dependents of the kernel
+  // before them: they launch early and wait on the device before reading
+  // its results. The select launches normally: making it a dependent of the
+  // previous step's seal as well let three grids queue ahead of each other
+  // and cost 29 us per step on a B200, while the two links save 3.6 us.
   sa_status st;
-  if ((st = ctx_select(c, query, kv_new, kv_fp32)) != SA_OK) return st;
-  if ((st = ctx_attend(c, query, out, 1)) != SA_OK) return st;
+  if ((st = ctx_select(c, query, kv_new, kv_fp32, false)) != SA_OK) return st;
+  if ((st = ctx_attend(c, query, out, 1, true)) != SA_OK) return st;
   ++c->launches;
-  return launch_seal(c->dev, 1, c->stream);
+  return launch_seal(c->dev, 1, c->stream, true);
 }
 
 SA_API sa_status sa_ctx_step_host(sa_ctx* c, const float* query_host, const void* kv_new_host,

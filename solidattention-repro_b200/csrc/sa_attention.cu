@@ -297,6 +297,7 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
   const uint8_t* pool = reinterpret_cast<const uint8_t*>(p.pool);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  pdl_launch_dependents();
 
   // ---- this CTA's slot range, its segments and its stage table ----
   const long long E = p.slots_per_unit;
@@ -340,6 +341,7 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
     mbar_fence_init();
     if constexpr (!kHeadMajor) tma_prefetch_desc(&map);
   }
+  pdl_wait();  // the selection (and the append) of this step
   for (int i = threadIdx.x; i < n; i += kThreads) {
     const long long x = lo + i;
     const int u = (int)(x / E);
@@ -645,7 +647,9 @@ sa_status launch_layout(const AttnParams& p, const CUtensorMap& map, cudaStream_
   const sa_status st =
       ensure_smem_limit((const void*)attention_kernel<G, kHeadMajor>, (int)smem, configured);
   if (st != SA_OK) return st;
-  attention_kernel<G, kHeadMajor><<<p.ctas, kThreads, smem, stream>>>(map, p);
+  const cudaError_t e = launch_kernel(attention_kernel<G, kHeadMajor>, dim3(p.ctas), dim3(kThreads),
+                                      smem, stream, p.pdl != 0, map, p);
+  if (e != cudaSuccess) return cuda_status(e, "attention_kernel launch");
   return cuda_status(cudaGetLastError(), "attention_kernel launch");
 }
 

@@ -164,6 +164,18 @@ __device__ __forceinline__ int block_exclusive_scan(int value, int* scratch, int
   return before;
 }
 
+// ---- programmatic dependent launch ------------------------------------------
+
+// Lets the next kernel of the stream launch (its CTAs become resident and run
+// up to their own pdl_wait) before this grid completes.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// Blocks until the preceding grid of the stream has completed and its memory
+// is visible; returns at once when the kernel was launched without the
+// programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---- decode-tail append ------------------------------------------------------
 
 // Writes the step's K/V of KV heads [kvh0, kvh1) of sequence-layer sl into

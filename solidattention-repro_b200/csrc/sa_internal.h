@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "sa_b200.h"
 
@@ -28,6 +29,25 @@ sa_status cuda_status(cudaError_t err, const char* what);
   } while (0)
 
 // Raises a kernel's dynamic shared memory limit to `bytes` once per device.
+// Launches kernel<<<grid, block, smem, stream>>>(args...), with programmatic
+// stream serialization when pdl is set (the kernel must pdl_wait before
+// reading what the preceding kernel wrote).
+template <class... KArgs, class... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t stream, bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 sa_status ensure_smem_limit(const void* kernel, int bytes, int* configured_per_device);
 constexpr int kMaxDevices = 64;
 
@@ -87,6 +107,7 @@ struct AttnParams {
   int fixed_tail_block;
   int fixed_tail_len;
   int tail_pending;    // tokens appended this step but not yet counted in tail_len
+  int pdl;             // launched as a programmatic dependent of the previous kernel
   const float* query;  // [num_sl][kv_heads*group][128]
   void* out;           // [num_sl][kv_heads*group][128]
   int out_fp16;
@@ -150,6 +171,7 @@ struct SelectParams {
   CtxDev append_ctx;
   const void* append_kv;  // [num_sl][2][kv_heads][128] FP16, or FP32 when append_kv_fp32
   int append_kv_fp32;
+  int pdl;  // launched as a programmatic dependent of the previous kernel
 };
 
 int select_max_blocks();
@@ -191,7 +213,7 @@ sa_status launch_append(const CtxDev& c, const float* query, const void* kv_new,
 // Rebuild the representative of every full tail and commit the seals.
 // pending = tokens appended by a fused append and not yet in tail_len (the
 // commit then stores every tail's new length).
-sa_status launch_seal(const CtxDev& c, int pending, cudaStream_t stream);
+sa_status launch_seal(const CtxDev& c, int pending, cudaStream_t stream, bool pdl = false);
 sa_status launch_pack_kv(uint16_t* packed, const float* key, const float* value,
                          size_t token, size_t elements, cudaStream_t stream);
 sa_status launch_xor(const uint8_t* in, uint8_t* out, size_t bytes, uint8_t mask,

@@ -294,6 +294,8 @@ __device__ void seal_commit(const CtxDev& c, int pending) {
 // seals (an atomic arrival count, reset by that CTA; no spinning).
 __global__ void __launch_bounds__(kRepThreads) seal_kernel(const CtxDev c, int pending) {
   __shared__ int last;
+  pdl_launch_dependents();
+  pdl_wait();  // the attention of this step still reads the tails
   const int items = c.qh * c.num_sl;
   for (int i = blockIdx.x; i < items; i += gridDim.x) {
     seal_rebuild(c, i % c.qh, i / c.qh, pending);
@@ -399,7 +401,7 @@ sa_status launch_append(const CtxDev& c, const float* query, const void* kv_new,
   return cuda_status(cudaGetLastError(), "append_kernel launch");
 }
 
-sa_status launch_seal(const CtxDev& c, int pending, cudaStream_t stream) {
+sa_status launch_seal(const CtxDev& c, int pending, cudaStream_t stream, bool pdl) {
   sa_status st = check_rep_params(kHeadDim, c.rep_window, c.rep_topk);
   if (st != SA_OK) return st;
   if ((st = ensure_smem_limit((const void*)seal_kernel, (int)sizeof(RepSmem), g_seal_smem)) != SA_OK)
@@ -407,8 +409,9 @@ sa_status launch_seal(const CtxDev& c, int pending, cudaStream_t stream) {
   // two CTAs per SM at most: an idle step (no full tail) costs one short wave
   const int items = c.qh * c.num_sl;
   const int grid = std::max(1, std::min(items, 2 * 148));
-  seal_kernel<<<grid, kRepThreads, sizeof(RepSmem), stream>>>(c, pending);
-  return cuda_status(cudaGetLastError(), "seal_kernel launch");
+  return cuda_status(launch_kernel(seal_kernel, dim3(grid), dim3(kRepThreads), sizeof(RepSmem),
+                                   stream, pdl, c, pending),
+                     "seal_kernel launch");
 }
 
 sa_status launch_pack_kv(uint16_t* packed, const float* key, const float* value, size_t token,

@@ -108,6 +108,8 @@ __global__ void __launch_bounds__(kThreads)
   // CTA) order keys [nb_cap]
   extern __shared__ float smem[];
   __shared__ TopkShared ts;
+  pdl_launch_dependents();
+  pdl_wait();  // sealed counts, tails and representatives of the previous step
   const int unit = blockIdx.y;
   const int sl = unit / p.n_groups;
   const int g = unit - sl * p.n_groups;
@@ -298,7 +300,8 @@ sa_status launch_select(const SelectParams& p, cudaStream_t stream) {
   if (st != SA_OK) return st;
   const int nchunks = std::max(1, (p.nb_cap + chunk - 1) / chunk);
   const dim3 grid(nchunks, p.num_sl * p.n_groups);
-  select_kernel<<<grid, kThreads, smem, stream>>>(p, vec);
+  const cudaError_t e = launch_kernel(select_kernel, grid, dim3(kThreads), smem, stream, p.pdl != 0, p, vec);
+  if (e != cudaSuccess) return cuda_status(e, "select_kernel launch");
   return cuda_status(cudaGetLastError(), "select_kernel launch");
 }
 
