@@ -360,15 +360,15 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
     s.ent_ntok[i] = (uint8_t)ntok;
   }
   __syncthreads();
-  if (threadIdx.x < s.nseg) {
-    const int k = threadIdx.x;
+  // stage table, one stage per thread
+  for (int j = threadIdx.x; j < s.nstages; j += kThreads) {
+    int k = 0;
+    while (k + 1 < s.nseg && s.seg_stage0[k + 1] <= j) ++k;
     const int j0 = s.seg_stage0[k], j1 = s.seg_stage0[k + 1];
     const int send = s.seg_slot0[k + 1];
-    for (int j = j0; j < j1; ++j) {
-      const int e0 = s.seg_slot0[k] + 2 * (j - j0);
-      s.stage_info[j] = stage_word(s.ent_ntok[e0], e0 + 1 < send ? s.ent_ntok[e0 + 1] : 0, e0,
-                                   k, j == j0, j + 1 == j1);
-    }
+    const int e0 = s.seg_slot0[k] + 2 * (j - j0);
+    s.stage_info[j] = stage_word(s.ent_ntok[e0], e0 + 1 < send ? s.ent_ntok[e0 + 1] : 0, e0, k,
+                                 j == j0, j + 1 == j1);
   }
   __syncthreads();
   const int nstages = s.nstages;
