@@ -11,7 +11,8 @@
 // unit owns `slots_per_unit` entry slots; slots past its entries are empty.
 //
 // Persistent schedule: the flattened slot list of all units is cut into one
-// contiguous range per CTA (about one wave). A CTA streams its range across
+// contiguous range per (virtual) CTA, about one wave: two 256-thread virtual
+// CTAs per 512-thread CTA and SM (see virt_ctas). A CTA streams its range across
 // unit boundaries without draining its load pipeline; the part of its range
 // inside one unit is a segment. The (physical block, token count) pair of
 // every slot in the range is resolved once, in parallel, into shared memory.
@@ -76,6 +77,27 @@ __host__ __device__ constexpr uint32_t stage_word(int ntok0, int ntok1, int e0, 
 __device__ __forceinline__ int info_ntok(uint32_t w, int i) { return (w >> (6 * i)) & 0x3f; }
 __device__ __forceinline__ int info_e0(uint32_t w) { return (w >> 12) & 0x1ff; }
 __device__ __forceinline__ int info_seg(uint32_t w) { return (w >> 21) & 0x1f; }
+
+// Virtual CTAs: with up to four query heads per KV head, one 512-thread CTA
+// runs two independent 256-thread halves ("virtual CTAs", each with its own
+// shared-memory state and named barrier), one per SM. Two separate CTAs per
+// SM would also fit, but the warp scheduler favours the older CTA: on a
+// B200 the second CTA of every SM finished ~20% later and then streamed
+// alone. The halves of one CTA are scheduled evenly, which balances the
+// SM's two shares of the work without changing the work split or any
+// result bit.
+template <int G>
+constexpr int virt_ctas() { return G <= 4 ? 2 : 1; }
+template <int V>
+__device__ __forceinline__ int vtid() { return V == 1 ? (int)threadIdx.x : (int)(threadIdx.x & 255); }
+template <int V>
+__device__ __forceinline__ int vhalf() { return V == 1 ? 0 : (int)(threadIdx.x >> 8); }
+template <int V>
+__device__ __forceinline__ int vbid() { return (int)blockIdx.x * V + vhalf<V>(); }
+template <int V>
+__device__ __forceinline__ void vsync() {
+  asm volatile("bar.sync %0, 256;" ::"r"(1 + vhalf<V>()) : "memory");
+}
 
 template <int G>
 struct alignas(128) AttnSmem {
@@ -241,7 +263,7 @@ __device__ __forceinline__ void store_out(const AttnParams& p, AttnSmem<G>& s, s
 // before thread 0's system-scope fence and atomics.
 template <int G>
 __device__ __forceinline__ void gather_push(const AttnParams& p, AttnSmem<G>& s, int u) {
-  __syncthreads();
+  vsync<virt_ctas<G>()>();
   const int esz = p.out_fp16 ? 2 : 4;
   const int chunks = G * kHeadDim * esz / 16;
   const int sl = u / p.kv_heads;
@@ -249,14 +271,14 @@ __device__ __forceinline__ void gather_push(const AttnParams& p, AttnSmem<G>& s,
   const size_t off = p.gather_slot_bytes +
                      (((size_t)sl * p.gather_world + p.gather_rank) * p.kv_heads + kvh) *
                          (size_t)(G * kHeadDim * esz);
-  for (int i = threadIdx.x; i < chunks * p.gather_world; i += kThreads) {
+  for (int i = vtid<virt_ctas<G>()>(); i < chunks * p.gather_world; i += kThreads) {
     const int r = i / chunks;
     const int c = i - r * chunks;
     uint8_t* dst = reinterpret_cast<uint8_t*>(p.gather_peers[r]) + off + (size_t)c * 16;
     *reinterpret_cast<uint4*>(dst) = reinterpret_cast<const uint4*>(s.ostage)[c];
   }
-  __syncthreads();
-  if (threadIdx.x == 0) {
+  vsync<virt_ctas<G>()>();
+  if (vtid<virt_ctas<G>()>() == 0) {
     __threadfence_system();
     for (int r = 0; r < p.gather_world; ++r)
       atomicAdd_system(reinterpret_cast<unsigned long long*>(
@@ -286,26 +308,28 @@ __device__ __forceinline__ void pv_tokens(const uint8_t* vrow, const float2 (*pb
 }
 
 template <int G, bool kHeadMajor>
-__global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
+__global__ void __launch_bounds__(kThreads * virt_ctas<G>(), 1)
     attention_kernel(const __grid_constant__ CUtensorMap map, const AttnParams p) {
   // Pairs (token, head) per half-warp: 4G over 16 lanes -> VPL per lane.
   constexpr int NPH = 4 * G;
   constexpr int VPL = NPH > 16 ? NPH / 16 : 1;
   constexpr int kPairShift = NPH >= 16 ? 0 : (NPH == 8 ? 1 : 2);  // lanes per pair = 1 << shift
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  AttnSmem<G>& s = *reinterpret_cast<AttnSmem<G>*>(smem_raw);
+  if (vbid<virt_ctas<G>()>() >= p.ctas) return;  // the idle half of an odd plan
+  AttnSmem<G>& s = *reinterpret_cast<AttnSmem<G>*>(
+      smem_raw + (size_t)vhalf<virt_ctas<G>()>() * sizeof(AttnSmem<G>));
   const uint8_t* pool = reinterpret_cast<const uint8_t*>(p.pool);
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
+  const int warp = vtid<virt_ctas<G>()>() >> 5;
+  const int lane = vtid<virt_ctas<G>()>() & 31;
   pdl_launch_dependents();
 
   // ---- this CTA's slot range, its segments and its stage table ----
   const long long E = p.slots_per_unit;
   const long long total = (long long)p.num_sl * p.kv_heads * E;
-  const long long lo = (long long)blockIdx.x * total / gridDim.x;
-  const long long hi = (long long)(blockIdx.x + 1) * total / gridDim.x;
+  const long long lo = (long long)vbid<virt_ctas<G>()>() * total / p.ctas;
+  const long long hi = (long long)(vbid<virt_ctas<G>()>() + 1) * total / p.ctas;
   const int n = (int)min(hi - lo, (long long)kMaxCtaSlots);
-  if (threadIdx.x == 0) {
+  if (vtid<virt_ctas<G>()>() == 0) {
     if (hi - lo > kMaxCtaSlots) raise_status(p.status, SA_DEV_BAD_BLOCK);
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&s.full[i], 1);
@@ -322,10 +346,10 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
         const long long u = u0 + k;
         const int a = (int)(max(lo, u * E) - lo);
         const int b = (int)(min(lo + n, (u + 1) * E) - lo);
-        const int cf = cta_of_slot(u * E, total, gridDim.x);
-        const int cl = cta_of_slot((u + 1) * E - 1, total, gridDim.x);
+        const int cf = cta_of_slot(u * E, total, p.ctas);
+        const int cl = cta_of_slot((u + 1) * E - 1, total, p.ctas);
         s.seg_unit[k] = (int)u;
-        s.seg_index[k] = (int)blockIdx.x - cf;
+        s.seg_index[k] = (int)vbid<virt_ctas<G>()>() - cf;
         s.seg_count[k] = cl - cf + 1;
         s.seg_slot0[k] = a;
         s.seg_stage0[k] = stages;
@@ -342,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
     if constexpr (!kHeadMajor) tma_prefetch_desc(&map);
   }
   pdl_wait();  // the selection (and the append) of this step
-  for (int i = threadIdx.x; i < n; i += kThreads) {
+  for (int i = vtid<virt_ctas<G>()>(); i < n; i += kThreads) {
     const long long x = lo + i;
     const int u = (int)(x / E);
     const int e = (int)(x - (long long)u * E);
@@ -359,9 +383,9 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
     s.ent_phys[i] = phys;
     s.ent_ntok[i] = (uint8_t)ntok;
   }
-  __syncthreads();
+  vsync<virt_ctas<G>()>();
   // stage table, one stage per thread
-  for (int j = threadIdx.x; j < s.nstages; j += kThreads) {
+  for (int j = vtid<virt_ctas<G>()>(); j < s.nstages; j += kThreads) {
     int k = 0;
     while (k + 1 < s.nseg && s.seg_stage0[k + 1] <= j) ++k;
     const int j0 = s.seg_stage0[k], j1 = s.seg_stage0[k + 1];
@@ -370,9 +394,9 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
     s.stage_info[j] = stage_word(s.ent_ntok[e0], e0 + 1 < send ? s.ent_ntok[e0 + 1] : 0, e0, k,
                                  j == j0, j + 1 == j1);
   }
-  __syncthreads();
+  vsync<virt_ctas<G>()>();
   const int nstages = s.nstages;
-  if (threadIdx.x == 0)
+  if (vtid<virt_ctas<G>()>() == 0)
     for (int j = 0; j < min(kStages, nstages); ++j)
       issue_stage<G, kHeadMajor>(s, &map, pool, p.kv_heads, j);
 
@@ -504,7 +528,7 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
 
     if (info & kInfoEnd) {
       // ---- segment end: merge the 8 warps through this stage's buffer ----
-      __syncthreads();  // every warp is done reading the stage
+      vsync<virt_ctas<G>()>();  // every warp is done reading the stage
       float* accw = reinterpret_cast<float*>(s.tiles[stage]);  // [8][G][128]
       // the two half-warps hold different tokens of the same dims
 #pragma unroll
@@ -536,9 +560,9 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
               make_float4(acc[g][2].x, acc[g][2].y, acc[g][3].x, acc[g][3].y);
         }
       }
-      __syncthreads();
-      if (threadIdx.x < G) {
-        const int g = threadIdx.x;
+      vsync<virt_ctas<G>()>();
+      if (vtid<virt_ctas<G>()>() < G) {
+        const int g = vtid<virt_ctas<G>()>();
         float M = -INFINITY;
         for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, s.mw[w][g]);
         float L = 0.f;
@@ -550,13 +574,13 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
         s.cta_m[g] = M;
         s.cta_l[g] = L;
       }
-      __syncthreads();
+      vsync<virt_ctas<G>()>();
       const int seg = info_seg(info);
       const int u = s.seg_unit[seg];
       const size_t out_base = (size_t)u * G * kHeadDim;
       const int nparts = s.seg_count[seg];
       if (nparts == 1) {
-        for (int idx = threadIdx.x; idx < G * kHeadDim; idx += kThreads) {
+        for (int idx = vtid<virt_ctas<G>()>(); idx < G * kHeadDim; idx += kThreads) {
           const int g = idx / kHeadDim, d = idx % kHeadDim;
           float o = 0.f;
 #pragma unroll
@@ -569,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
       } else {
         float* part =
             p.partial + ((size_t)u * p.max_segments + s.seg_index[seg]) * G * kPartialStride;
-        for (int idx = threadIdx.x; idx < G * kHeadDim; idx += kThreads) {
+        for (int idx = vtid<virt_ctas<G>()>(); idx < G * kHeadDim; idx += kThreads) {
           const int g = idx / kHeadDim, d = idx % kHeadDim;
           float o = 0.f;
 #pragma unroll
@@ -581,17 +605,17 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
             part[g * kPartialStride + 1] = s.cta_l[g];
           }
         }
-        __syncthreads();
-        if (threadIdx.x == 0) {
+        vsync<virt_ctas<G>()>();
+        if (vtid<virt_ctas<G>()>() == 0) {
           // the barrier orders the CTA's partial stores before this fence
           __threadfence();
           s.last_flag = atomicAdd(&p.counters[u], 1) == nparts - 1;
           if (s.last_flag) __threadfence();
         }
-        __syncthreads();
+        vsync<virt_ctas<G>()>();
         if (s.last_flag) {
           const float* parts = p.partial + (size_t)u * p.max_segments * G * kPartialStride;
-          for (int idx = threadIdx.x; idx < G * kHeadDim; idx += kThreads) {
+          for (int idx = vtid<virt_ctas<G>()>(); idx < G * kHeadDim; idx += kThreads) {
             const int g = idx / kHeadDim, d = idx % kHeadDim;
             float M = -INFINITY;
             for (int k = 0; k < nparts; ++k)
@@ -607,11 +631,11 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
             }
             store_out<G>(p, s, out_base, idx, L > 0.f ? o / L : 0.f);
           }
-          if (threadIdx.x == 0) p.counters[u] = 0;
+          if (vtid<virt_ctas<G>()>() == 0) p.counters[u] = 0;
           if (p.gather_peers) gather_push<G>(p, s, u);
         }
       }
-      __syncthreads();  // the stage buffer is free again
+      vsync<virt_ctas<G>()>();  // the stage buffer is free again
     }
 
     // Release the stage; its last user refills it with stage j + kStages.
@@ -631,8 +655,8 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
     }
   }
 
-  __syncthreads();
-  if (s.abort_flag && threadIdx.x == 0) {
+  vsync<virt_ctas<G>()>();
+  if (s.abort_flag && vtid<virt_ctas<G>()>() == 0) {
     // Let the loads still in flight land (bounded) before the CTA exits.
     for (int st = 0; st < kStages; ++st)
       if (s.stage_issues[st] > 0)
@@ -642,12 +666,14 @@ __global__ void __launch_bounds__(kThreads, (G <= 4 ? 2 : 1))
 
 template <int G, bool kHeadMajor>
 sa_status launch_layout(const AttnParams& p, const CUtensorMap& map, cudaStream_t stream) {
-  const size_t smem = sizeof(AttnSmem<G>);
+  constexpr int kV = virt_ctas<G>();
+  const size_t smem = kV * sizeof(AttnSmem<G>);
   static int configured[kMaxDevices];
   const sa_status st =
       ensure_smem_limit((const void*)attention_kernel<G, kHeadMajor>, (int)smem, configured);
   if (st != SA_OK) return st;
-  const cudaError_t e = launch_kernel(attention_kernel<G, kHeadMajor>, dim3(p.ctas), dim3(kThreads),
+  const cudaError_t e = launch_kernel(attention_kernel<G, kHeadMajor>, dim3((p.ctas + kV - 1) / kV),
+                                      dim3(kThreads * kV),
                                       smem, stream, p.pdl != 0, map, p);
   if (e != cudaSuccess) return cuda_status(e, "attention_kernel launch");
   return cuda_status(cudaGetLastError(), "attention_kernel launch");
