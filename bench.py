@@ -440,6 +440,20 @@ def main():
            "d2h_bytes_per_step": out_host.numel() * out_host.element_size() + 4,
            "steps": e2e_steps, "timing": "host wall clock around synchronous calls, max over ranks"}
 
+    # ---- selection quality of the last step (dense audit, not timed)
+    from solidattention_repro_b200 import quality as quality_mod
+    ctx.select(q_last)
+    mass = ctx.audit(q_last)
+    ctx.sync()
+    hot = info["hot"]
+    if heads_mode:
+        hot = hot[:, :, kv_slice[0]:kv_slice[0] + kv_slice[1]]
+    qual = quality_mod.selection_quality(
+        mass.cpu().numpy(), ctx.selected.cpu().numpy(), ctx.selected_count.cpu().numpy(),
+        ctx.num_sealed.cpu().numpy(), w.budget_blocks, w.init_blocks, w.local_blocks,
+        hot.reshape(ctx.num_sl, ctx.kh, -1) if w.hot_blocks else None)
+    del mass
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = run_cpu_baseline(ctx, w, q_last, w.layers, args.cpu_seconds, os.cpu_count() or 1)
@@ -477,6 +491,7 @@ def main():
                               "frac": attn_gbs / hbm},
                 "select": {"ms": t_sel, "bytes": rep_bytes, "gbs": sel_gbs,
                            "frac": sel_gbs / hbm}},
+            "quality": qual,
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": gpu_launches,
             "device_status_bits": phase_bits,
             "clocks": clock_info,

@@ -312,6 +312,17 @@ SA_API sa_status sa_ctx_seal(sa_ctx* ctx);
 SA_API sa_status sa_ctx_sync(sa_ctx* ctx, uint32_t* bits_out);
 /* Kernel launches issued by the context since creation (for accounting). */
 SA_API uint64_t sa_ctx_launch_count(const sa_ctx* ctx);
+/* Quality audit of the selection (replaces audit_dense_selection,
+ * cpp/src/pipeline_main.cpp:502-574, and the selected-vs-dense comparison of
+ * cpp/src/selection_main.cpp:246-252): for every (seq, layer, KV head), the
+ * dense softmax of the KV head's query heads over all sealed blocks plus the
+ * open tail, summed per block and averaged over those heads.
+ *   query    [seqs][layers][QH][D] FP32 (device);
+ *   mass_out [seqs*layers][KH][table_blocks + 1] FP32 (device): entry b <
+ *            num_sealed = sealed block b, entry table_blocks = the tail,
+ *            others 0; each row sums to 1 (when the row has tokens).
+ * Asynchronous on the context stream; not part of the decode step. */
+SA_API sa_status sa_ctx_audit(sa_ctx* ctx, const float* query, float* mass_out);
 
 /* ---- KV-head-sharded contexts: outputs gathered over peer memory ---------
  * No reference counterpart as a function: replaces the all-gather of

@@ -371,6 +371,15 @@ class DecodeContext:
         self._lib.sa_ctx_sync(self._h, C.byref(bits))
         return int(bits.value)
 
+    def audit(self, query: torch.Tensor) -> torch.Tensor:
+        """Dense attention mass per block [S*L, KH, table_blocks + 1] (the last
+        entry = the open tail) for this query; see sa_ctx_audit."""
+        mass = torch.empty(self.num_sl, self.kh, self.table_blocks + 1, device=self.device,
+                           dtype=torch.float32)
+        check(self._lib.sa_ctx_audit(self._h, _dev_ptr(query, torch.float32, "query"),
+                                     mass.data_ptr()), "sa_ctx_audit")
+        return mass
+
     @property
     def launches(self) -> int:
         return int(self._lib.sa_ctx_launch_count(self._h))

@@ -1013,6 +1013,13 @@ SA_API sa_status sa_ctx_sync(sa_ctx* c, uint32_t* bits_out) {
 
 SA_API uint64_t sa_ctx_launch_count(const sa_ctx* c) { return c ? c->launches : 0; }
 
+SA_API sa_status sa_ctx_audit(sa_ctx* c, const float* query, float* mass_out) {
+  if (!c || !query || !mass_out) return fail(SA_ERR_INVALID_ARG, "audit: null argument");
+  DeviceGuard guard(c->cfg.device);
+  ++c->launches;
+  return launch_audit(c->dev, query, mass_out, c->cfg.scale, c->stream);
+}
+
 // ------------------------------------------- KV-head-sharded gather over peer memory
 
 SA_API sa_status sa_ctx_gather_buffer(sa_ctx* c, int32_t world, void** buf_out,

@@ -214,6 +214,11 @@ sa_status launch_append(const CtxDev& c, const float* query, const void* kv_new,
 // pending = tokens appended by a fused append and not yet in tail_len (the
 // commit then stores every tail's new length).
 sa_status launch_seal(const CtxDev& c, int pending, cudaStream_t stream, bool pdl = false);
+// Dense attention mass per block of every (seq-layer, KV head), averaged
+// over the KV head's query heads: mass [num_sl][kv_heads][table_blocks + 1],
+// entry table_blocks = the open tail (sa_audit.cu).
+sa_status launch_audit(const CtxDev& c, const float* query, float* mass, float scale,
+                       cudaStream_t stream);
 sa_status launch_pack_kv(uint16_t* packed, const float* key, const float* value,
                          size_t token, size_t elements, cudaStream_t stream);
 sa_status launch_xor(const uint8_t* in, uint8_t* out, size_t bytes, uint8_t mask,
