@@ -143,6 +143,7 @@ struct sa_ctx {
   void* d_kv_new = nullptr;
   void* d_out = nullptr;
   uint32_t* h_status = nullptr;  // pinned
+  uint32_t* h_status_dev = nullptr;  // its device-side address
   std::vector<uint8_t> prefilled;
   uint64_t launches = 0;
   // KV-head-sharded gather over peer memory: two parity slots of
@@ -771,6 +772,10 @@ SA_API sa_status sa_ctx_create(const sa_ctx_config* config, sa_ctx** out) {
     st = cuda_status(cudaHostAlloc(reinterpret_cast<void**>(&c->h_status), sizeof(uint32_t),
                                    cudaHostAllocDefault),
                      "cudaHostAlloc status");
+  if (st == SA_OK)
+    st = cuda_status(cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->h_status_dev),
+                                              c->h_status, 0),
+                     "cudaHostGetDevicePointer status");
   // The pool is head-major and read with bulk copies: no tensor map.
   std::memset(&c->pool_map, 0, sizeof(c->pool_map));
   if (st == SA_OK) {
@@ -957,10 +962,27 @@ SA_API sa_status sa_ctx_seal(sa_ctx* c) {
   return launch_seal(c->dev, 0, c->stream);
 }
 
+}  // extern "C"
+
+namespace {
+sa_status ctx_step(sa_ctx* c, const float* query, const void* kv_new, int32_t kv_fp32, void* out,
+                   uint32_t* status_mirror);
+}
+
+extern "C" {
+
 SA_API sa_status sa_ctx_step(sa_ctx* c, const float* query, const void* kv_new, int32_t kv_fp32,
                              void* out) {
   if (!c || !query || !kv_new || !out) return fail(SA_ERR_INVALID_ARG, "step: null argument");
   DeviceGuard guard(c->cfg.device);
+  return ctx_step(c, query, kv_new, kv_fp32, out, nullptr);
+}
+
+}  // extern "C"
+
+namespace {
+sa_status ctx_step(sa_ctx* c, const float* query, const void* kv_new, int32_t kv_fp32, void* out,
+                   uint32_t* status_mirror) {
   // Three launches: select with the fused append (the new token is written
   // but not yet counted in tail_len), attention counting that pending token,
   // then the seal kernel, which rebuilds full tails and stores every tail's
@@ -973,8 +995,25 @@ SA_API sa_status sa_ctx_step(sa_ctx* c, const float* query, const void* kv_new, 
   if ((st = ctx_select(c, query, kv_new, kv_fp32, false)) != SA_OK) return st;
   if ((st = ctx_attend(c, query, out, 1, true)) != SA_OK) return st;
   ++c->launches;
-  return launch_seal(c->dev, 1, c->stream, true);
+  CtxDev d = c->dev;
+  d.status_mirror = status_mirror;
+  return launch_seal(d, 1, c->stream, true);
 }
+
+// Device-side address of a pinned, mapped host buffer aligned to `align`
+// bytes, or null (pageable memory, or an unaligned pointer).
+void* mapped_host(const void* p, uintptr_t align) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (a.type != cudaMemoryTypeHost || !a.devicePointer) return nullptr;
+  if (reinterpret_cast<uintptr_t>(a.devicePointer) % align) return nullptr;
+  return a.devicePointer;
+}
+}  // namespace
+extern "C" {
 
 SA_API sa_status sa_ctx_step_host(sa_ctx* c, const float* query_host, const void* kv_new_host,
                                   int32_t kv_fp32, void* out_host) {
@@ -985,14 +1024,27 @@ SA_API sa_status sa_ctx_step_host(sa_ctx* c, const float* query_host, const void
   const size_t q_bytes = (size_t)c->num_sl * g.query_heads * kHeadDim * sizeof(float);
   const size_t kv_bytes = (size_t)c->num_sl * c->dev.row_elems * (kv_fp32 ? 4 : 2);
   const size_t out_bytes = (size_t)c->num_sl * g.query_heads * kHeadDim * (g.out_fp16 ? 2 : 4);
+  // Pinned, mapped caller buffers are used in place: the fused append reads
+  // the new K/V from host memory, the attention writes the output there and
+  // the seal copies the status word to a mapped host word, so only the
+  // queries (read by every scoring CTA) are copied. Pageable buffers go
+  // through device staging copies.
+  void* kv_dev = mapped_host(kv_new_host, 16);
+  void* out_dev = mapped_host(out_host, 16);
   SA_CUDA_TRY(cudaMemcpyAsync(c->d_query, query_host, q_bytes, cudaMemcpyHostToDevice, c->stream));
-  SA_CUDA_TRY(cudaMemcpyAsync(c->d_kv_new, kv_new_host, kv_bytes, cudaMemcpyHostToDevice, c->stream));
-  sa_status st = sa_ctx_step(c, c->d_query, c->d_kv_new, kv_fp32, c->d_out);
+  if (!kv_dev) {
+    SA_CUDA_TRY(cudaMemcpyAsync(c->d_kv_new, kv_new_host, kv_bytes, cudaMemcpyHostToDevice, c->stream));
+    kv_dev = c->d_kv_new;
+  }
+  *reinterpret_cast<volatile uint32_t*>(c->h_status) = 0xffffffffu;  // "not written"
+  sa_status st = ctx_step(c, c->d_query, kv_dev, kv_fp32, out_dev ? out_dev : c->d_out,
+                          c->h_status_dev);
   if (st != SA_OK) return st;
-  SA_CUDA_TRY(cudaMemcpyAsync(out_host, c->d_out, out_bytes, cudaMemcpyDeviceToHost, c->stream));
-  SA_CUDA_TRY(cudaMemcpyAsync(c->h_status, c->dev.status, sizeof(uint32_t), cudaMemcpyDeviceToHost,
-                              c->stream));
+  if (!out_dev)
+    SA_CUDA_TRY(cudaMemcpyAsync(out_host, c->d_out, out_bytes, cudaMemcpyDeviceToHost, c->stream));
   SA_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  if (*reinterpret_cast<volatile uint32_t*>(c->h_status) == 0xffffffffu)
+    SA_CUDA_TRY(cudaMemcpy(c->h_status, c->dev.status, sizeof(uint32_t), cudaMemcpyDeviceToHost));
   if (*c->h_status)
     return fail(*c->h_status & SA_DEV_TIMEOUT ? SA_ERR_TIMEOUT : SA_ERR_DEVICE,
                 "step_host: device status bits 0x" + std::to_string(*c->h_status));

@@ -77,6 +77,7 @@ struct CtxDev {
   int32_t* free_top;
   int* seal_counters;  // [1] arrivals of the seal kernel's CTAs
   uint32_t* status;
+  uint32_t* status_mirror;  // device-mapped host word the seal commit copies status to (nullable)
   int num_sl, qh, kv_heads;
   int rep_window, rep_topk;
   float rep_scale;

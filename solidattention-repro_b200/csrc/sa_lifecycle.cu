@@ -286,7 +286,16 @@ __device__ void seal_commit(const CtxDev& c, int pending) {
     taken_before += total;
   }
   __syncthreads();
-  if (threadIdx.x == 0) *c.free_top = max(0, base_top - taken_before);
+  if (threadIdx.x == 0) {
+    *c.free_top = max(0, base_top - taken_before);
+    if (c.status_mirror) {
+      // every kernel of the step has finished writing status bits by now
+      __threadfence();
+      *reinterpret_cast<volatile uint32_t*>(c.status_mirror) =
+          *reinterpret_cast<volatile uint32_t*>(c.status);
+      __threadfence_system();
+    }
+  }
 }
 
 // Grid-stride over (query head, sequence-layer) items: rebuild the

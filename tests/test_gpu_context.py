@@ -385,3 +385,41 @@ def test_selection_beats_random_on_planted_blocks(pkg, cuda):
     assert res["oracle_recall"] >= 1.3 * oracle_random
     assert w.budget_blocks / (nb + 1) < res["selected_mass"] <= 1.0 + 1e-5
     ctx.close()
+
+
+def test_step_host_matches_device_step_pinned_and_pageable(pkg, cuda):
+    """sa_ctx_step_host, the end-to-end call of a host decode loop, with
+    pinned mapped buffers (used in place: K/V read and output written over
+    the bus, status mirrored by the seal) and with pageable buffers (staged
+    copies): both equal the device-pointer step bit for bit, across a seal."""
+    import dataclasses
+
+    from solidattention_repro_b200 import workloads
+
+    w = dataclasses.replace(workloads.CONFIGS["cfg2"], name="host-step-test", layers=2,
+                            context_blocks=40, budget_blocks=12, hot_blocks=2)
+    steps = 34
+    ctxs = [workloads.make_context(w, steps, cuda, seed=6) for _ in range(3)]
+    q, kv = workloads.decode_inputs(w, ctxs[0][1], steps, cuda, seed=6)
+    q_pin = torch.empty(q[0].shape, dtype=torch.float32, pin_memory=True)
+    kv_pin = torch.empty(kv[0].shape, dtype=torch.float16, pin_memory=True)
+    out_pin = torch.empty(ctxs[0][0].new_output().shape, dtype=torch.float16, pin_memory=True)
+    for s in range(steps):
+        want = ctxs[0][0].step(q[s], kv[s]).cpu().numpy()
+        q_pin.copy_(q[s].cpu())
+        kv_pin.copy_(kv[s].cpu())
+        ctxs[1][0].step_host(q_pin, kv_pin, out_pin)
+        q_np, kv_np = q[s].cpu().numpy().copy(), kv[s].cpu().numpy().copy()
+        out_np = np.empty(want.shape, np.float16)
+        ctxs[2][0].step_host(q_np, kv_np, out_np)
+        assert np.array_equal(out_pin.numpy(), want), s
+        assert np.array_equal(out_np, want), s
+    for c, _ in ctxs:
+        assert c.status_bits() == 0
+    ref = ctxs[0][0]
+    for c, _ in ctxs[1:]:
+        for name in ("num_sealed", "tail_len", "tail_block", "generation", "selected"):
+            assert torch.equal(getattr(c, name), getattr(ref, name)), name
+    assert (ref.generation.cpu().numpy() == 1).all()  # the 32nd append sealed
+    for c, _ in ctxs:
+        c.close()
