@@ -70,14 +70,21 @@ def peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def profile_traffic(kernel: str, workload: str):
-    """DRAM bytes per launch recorded from an ncu capture in profiles/, or None."""
+def profile_traffic(kernel: str, workload: str, bytes_per_launch: int | None = None):
+    """DRAM bytes per launch from an ncu capture recorded in profiles/, or None.
+
+    A profile line reads `traffic_per_launch[kernel@workload]: T` or
+    `... : T per A algorithmic bytes`; with A given, T is scaled to
+    bytes_per_launch (traffic grows in proportion to the blocks processed)."""
     for f in sorted((ROOT / "profiles").glob("*.md")):
         text = f.read_text()
-        m = re.search(rf"traffic_per_launch\[{re.escape(kernel)}@{re.escape(workload)}\]:\s*([0-9.]+)",
-                      text)
+        m = re.search(rf"traffic_per_launch\[{re.escape(kernel)}@{re.escape(workload)}\]:\s*([0-9.]+)"
+                      rf"(?:\s+per\s+([0-9.]+)\s+algorithmic bytes)?", text)
         if m:
-            return float(m.group(1))
+            traffic = float(m.group(1))
+            if m.group(2) and bytes_per_launch:
+                traffic *= bytes_per_launch / float(m.group(2))
+            return traffic
     return None
 
 
@@ -387,7 +394,7 @@ def main():
     sel_gbs = rep_bytes / (t_sel * 1e-3) / 1e9
     dominant = ("attention", t_attn, attn_gbs, kv_bytes) if t_attn >= t_sel else \
         ("select", t_sel, sel_gbs, rep_bytes)
-    traffic = profile_traffic(dominant[0], args.config)
+    traffic = profile_traffic(dominant[0], args.config, dominant[3])
 
     # ---- end to end through the public host-buffer call
     qn = w.seqs * w.layers * ctx.qh * 128

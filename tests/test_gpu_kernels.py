@@ -132,6 +132,29 @@ def test_select_signed_zero_and_equal_scores(pkg, port, cuda):
     assert np.array_equal(ids.cpu().numpy(), want)
 
 
+@pytest.mark.parametrize("case", ["crowded_bucket", "infinite_score", "two_values"])
+def test_select_top_k_adversarial_scores(pkg, port, cuda, case):
+    """Adversarial score sets for the radix top-k: two far outliers above 1200
+    near-equal scores, an infinite score, and scores of only two values."""
+    rng = np.random.default_rng({"crowded_bucket": 1, "infinite_score": 2, "two_values": 3}[case])
+    qh, blocks, budget = 4, 1200, 100
+    q = rng.standard_normal((qh, 128), dtype=np.float32)
+    base = rng.standard_normal((qh, 1, 128), dtype=np.float32)
+    if case == "two_values":
+        reps = np.repeat(base, blocks, axis=1)
+        reps[:, ::3] = -reps[:, ::3]
+    else:
+        reps = base + rng.standard_normal((qh, blocks, 128), dtype=np.float32) * np.float32(1e-4)
+        reps[:, 7] *= 1e4
+        reps[:, 900] *= -1e4
+        if case == "infinite_score":
+            reps[:, 33] = np.float32(1e30) * np.sign(q)
+    reps = np.ascontiguousarray(reps.astype(np.float32))
+    want, _ = port.select_grouped(q, reps, qh, qh, blocks, 128, budget, 1, 2)
+    ids, _ = pkg.select_shared_blocks(_t(q, cuda), _t(reps, cuda), qh, blocks, 128, budget, 1, 2)
+    assert np.array_equal(ids.cpu().numpy(), want)
+
+
 def test_select_rejects_what_the_reference_rejects(pkg, cuda):
     q = torch.zeros(4, 128, device=cuda)
     reps = torch.zeros(4, 8, 128, device=cuda)

@@ -86,6 +86,11 @@ def test_profile_traffic_lookup(bench, tmp_path, monkeypatch):
     (tmp_path / "profiles").mkdir()
     (tmp_path / "profiles" / "x.md").write_text(
         "traffic_per_launch[attention@cfg3]: 605000000\n")
+    (tmp_path / "profiles" / "y.md").write_text(
+        "traffic_per_launch[select@cfg3]: 612000000 per 600000000 algorithmic bytes\n")
     monkeypatch.setattr(bench, "ROOT", tmp_path)
     assert bench.profile_traffic("attention", "cfg3") == 605000000.0
-    assert bench.profile_traffic("select", "cfg3") is None
+    # a capture of a 600 MB launch scaled to the timed 650 MB launch
+    assert bench.profile_traffic("select", "cfg3", 650_000_000) == 612000000 * 650 / 600
+    assert bench.profile_traffic("select", "cfg3") == 612000000.0
+    assert bench.profile_traffic("select", "cfg5") is None
