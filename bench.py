@@ -460,6 +460,19 @@ def main():
         ctx.num_sealed.cpu().numpy(), w.budget_blocks, w.init_blocks, w.local_blocks,
         hot.reshape(ctx.num_sl, ctx.kh, -1) if w.hot_blocks else None)
     del mass
+    # history prediction (the reference's tiered pipeline): a slot window that
+    # follows the selection of the last eight steps' queries
+    slots = ctx.new_slots()
+    hits = selected = 0
+    for k in range(8):
+        ctx.select(queries[total - 8 + k])
+        _, _, stats = ctx.slot_correct(slots)
+        if k:
+            st = stats.cpu().numpy()
+            hits += int(st[..., 0].sum())
+            selected += int(st.sum())
+    ctx.sync()
+    qual["history_hit_rate"] = hits / selected if selected else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -323,6 +323,23 @@ SA_API uint64_t sa_ctx_launch_count(const sa_ctx* ctx);
  *            others 0; each row sums to 1 (when the row has tokens).
  * Asynchronous on the context stream; not part of the decode step. */
 SA_API sa_status sa_ctx_audit(sa_ctx* ctx, const float* query, float* mass_out);
+/* History-prediction slot table (replaces compare_prediction,
+ * cpp/src/pipeline_main.cpp:686-717, and the slot maps of
+ * src/solidattention_lab/qwen_decode.py:463-545): a resident window of
+ * `budget` slots per (seq, layer, selection group) that holds the blocks
+ * predicted for this step (last step's selection). Against the context's
+ * current selection (after sa_ctx_select / sa_ctx_step): hits stay; the
+ * misses (selected blocks not resident, ascending) overwrite, in order, the
+ * slots whose block was not selected (in slot order); slots left over when
+ * the selection is shorter than the window are emptied. Empty slots are -1.
+ *   slots   [seqs*layers][groups][budget] int32, device, corrected in place;
+ *   misses  [seqs*layers][groups][budget] int32, device: blocks to load, -1 padded;
+ *   replace [seqs*layers][groups][budget] int32, device: the slot each miss
+ *           overwrites, -1 padded;
+ *   stats   [seqs*layers][groups][2] int32, device: hits, misses.
+ * Asynchronous on the context stream. */
+SA_API sa_status sa_ctx_slot_correct(sa_ctx* ctx, int32_t* slots, int32_t* misses,
+                                     int32_t* replace, int32_t* stats);
 
 /* ---- KV-head-sharded contexts: outputs gathered over peer memory ---------
  * No reference counterpart as a function: replaces the all-gather of

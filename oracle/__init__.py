@@ -211,6 +211,23 @@ class Port(_Lib):
         o = np.ascontiguousarray(offsets, np.int64).reshape(-1)
         return int(self.lib.sao_fnv_offsets(o, o.size))
 
+    def slot_correct(self, selected, counts, slots):
+        """compare_prediction per unit (see sao_slot_correct): returns the
+        corrected slots, misses, replacement slots and (hits, misses)."""
+        sel = np.ascontiguousarray(selected, np.int32)
+        units, budget = sel.shape
+        cnt = np.ascontiguousarray(counts, np.int32).reshape(units)
+        sl = np.array(slots, np.int32, copy=True).reshape(units, budget)
+        mi = np.empty_like(sl)
+        re = np.empty_like(sl)
+        st = np.empty((units, 2), np.int32)
+        P = C.c_void_p
+        self.lib.sao_slot_correct.argtypes = [P] * 6 + [_sz, _sz]
+        self.lib.sao_slot_correct.restype = None
+        self.lib.sao_slot_correct(sel.ctypes.data, cnt.ctypes.data, sl.ctypes.data, mi.ctypes.data,
+                                  re.ctypes.data, st.ctypes.data, units, budget)
+        return sl, mi, re, st
+
     def lifecycle_run(self, layers, q_heads, kv_heads, head_dim, block_tokens, local_tokens,
                       decode_tokens, initial_blocks, with_store=False, with_indices=False):
         class Res(C.Structure):

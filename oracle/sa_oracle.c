@@ -527,3 +527,43 @@ void sao_top4_first_max(const float* scores, size_t block_tokens, int64_t* out) 
     out[rank] = (int64_t)best;
   }
 }
+
+/* compare_prediction (cpp/src/pipeline_main.cpp:686-717): slots whose block
+ * is in the new selection are hits (:690-693); the other slots, in slot
+ * order, are freed (:694-696); selected blocks not resident, in selection
+ * order, are misses (:698-703); the i-th miss goes to the i-th freed slot
+ * (:708-710). Empty slots (-1) are never hits; freed slots beyond the misses
+ * are emptied (the reference has equal counts and throws otherwise,
+ * :704-706). */
+void sao_slot_correct(const int32_t* selected, const int32_t* counts, int32_t* slots,
+                      int32_t* misses, int32_t* replace, int32_t* stats, size_t units,
+                      size_t budget) {
+  for (size_t u = 0; u < units; ++u) {
+    const int32_t* sel = selected + u * budget;
+    int32_t* sl = slots + u * budget;
+    int32_t* mi = misses + u * budget;
+    int32_t* re = replace + u * budget;
+    size_t count = counts[u] < 0 ? 0 : (size_t)counts[u];
+    if (count > budget) count = budget;
+    size_t nfree = 0, nmiss = 0;
+    for (size_t s = 0; s < budget; ++s) mi[s] = re[s] = -1;
+    int32_t* freed = (int32_t*)malloc(budget * sizeof(int32_t));
+    for (size_t s = 0; s < budget; ++s) {
+      int hit = 0;
+      for (size_t i = 0; i < count && sl[s] >= 0; ++i) hit |= sel[i] == sl[s];
+      if (!hit) freed[nfree++] = (int32_t)s;
+    }
+    for (size_t i = 0; i < count; ++i) {
+      int resident = 0;
+      for (size_t s = 0; s < budget; ++s) resident |= sl[s] >= 0 && sl[s] == sel[i];
+      if (!resident) mi[nmiss++] = sel[i];
+    }
+    for (size_t k = 0; k < nfree; ++k) {
+      sl[freed[k]] = k < nmiss ? mi[k] : -1;
+      if (k < nmiss) re[k] = freed[k];
+    }
+    stats[2 * u] = (int32_t)(count - nmiss);
+    stats[2 * u + 1] = (int32_t)nmiss;
+    free(freed);
+  }
+}

@@ -21,6 +21,7 @@
  *   sao_gather_packed          cpp/src/selection_main.cpp:196-218 and
  *                              cpp/src/qwen_chain_main.cpp:360-395 (token order)
  *   sao_lifecycle_run          cpp/src/kv_lifecycle_main.cpp:25-113
+ *   sao_slot_correct           cpp/src/pipeline_main.cpp:686-717
  *
  * Parity of this restatement is pinned against the reference compiled from
  * its own sources (oracle/_ref) and against the reference's published known
@@ -135,6 +136,16 @@ int sao_sparse_step(const uint16_t* pool, const int32_t* table,
 /* The lifecycle's representative audit (kv_lifecycle_main.cpp:93-103): four
  * in-block offsets by descending score, first maximum wins. */
 void sao_top4_first_max(const float* scores, size_t block_tokens, int64_t* out);
+
+/* History-prediction slot correction, compare_prediction
+ * (cpp/src/pipeline_main.cpp:686-717) per unit, generalised to empty slots
+ * (-1, always overwritten) and to selections shorter than the window (the
+ * freed slots beyond the misses are emptied). selected [units][budget]
+ * ascending with counts [units]; slots [units][budget] corrected in place;
+ * misses / replace [units][budget] -1 padded; stats [units][2] = hits, misses. */
+void sao_slot_correct(const int32_t* selected, const int32_t* counts, int32_t* slots,
+                      int32_t* misses, int32_t* replace, int32_t* stats, size_t units,
+                      size_t budget);
 
 /* FNV-1a over 64-bit words, as the C2.1 driver hashes representative offsets
  * (cpp/src/selection_main.cpp:167-171). */

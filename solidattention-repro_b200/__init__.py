@@ -380,6 +380,25 @@ class DecodeContext:
                                      mass.data_ptr()), "sa_ctx_audit")
         return mass
 
+    def new_slots(self) -> torch.Tensor:
+        """An empty slot table [S*L, groups, budget] (-1) for slot_correct."""
+        return torch.full((self.num_sl, self.n_groups, self.budget), -1, dtype=torch.int32,
+                          device=self.device)
+
+    def slot_correct(self, slots: torch.Tensor):
+        """Correct `slots` in place against the current selection; returns
+        (misses, replace, stats) [S*L, groups, budget] / [..., 2] (see
+        sa_ctx_slot_correct)."""
+        if slots.shape != (self.num_sl, self.n_groups, self.budget) or slots.dtype != torch.int32:
+            raise ValueError("slots must be int32 [S*L, groups, budget]")
+        misses = torch.empty_like(slots)
+        replace = torch.empty_like(slots)
+        stats = torch.empty(self.num_sl, self.n_groups, 2, dtype=torch.int32, device=self.device)
+        check(self._lib.sa_ctx_slot_correct(self._h, slots.data_ptr(), misses.data_ptr(),
+                                            replace.data_ptr(), stats.data_ptr()),
+              "sa_ctx_slot_correct")
+        return misses, replace, stats
+
     @property
     def launches(self) -> int:
         return int(self._lib.sa_ctx_launch_count(self._h))

@@ -106,6 +106,7 @@ PROTOTYPES = {
     "sa_ctx_sync": (C.c_int, [_vp, C.POINTER(C.c_uint32)]),
     "sa_ctx_launch_count": (C.c_uint64, [_vp]),
     "sa_ctx_audit": (C.c_int, [_vp, _vp, _vp]),
+    "sa_ctx_slot_correct": (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
     "sa_ctx_gather_buffer": (C.c_int, [_vp, _i32, C.POINTER(_vp), C.POINTER(_sz)]),
     "sa_ctx_gather_attach": (C.c_int, [_vp, _i32, C.POINTER(_vp)]),
     "sa_ctx_gather_wait": (C.c_int, [_vp, C.POINTER(_vp)]),

@@ -1072,6 +1072,17 @@ SA_API sa_status sa_ctx_audit(sa_ctx* c, const float* query, float* mass_out) {
   return launch_audit(c->dev, query, mass_out, c->cfg.scale, c->stream);
 }
 
+SA_API sa_status sa_ctx_slot_correct(sa_ctx* c, int32_t* slots, int32_t* misses, int32_t* replace,
+                                     int32_t* stats) {
+  if (!c || !slots || !misses || !replace || !stats)
+    return fail(SA_ERR_INVALID_ARG, "slot_correct: null argument");
+  DeviceGuard guard(c->cfg.device);
+  ++c->launches;
+  return launch_slot_correct(c->selected, c->selected_count, slots, misses, replace, stats,
+                             c->num_sl * c->n_sel_groups, c->cfg.budget_blocks,
+                             c->cfg.table_blocks, c->dev.status, c->stream);
+}
+
 // ------------------------------------------- KV-head-sharded gather over peer memory
 
 SA_API sa_status sa_ctx_gather_buffer(sa_ctx* c, int32_t world, void** buf_out,

@@ -220,6 +220,10 @@ sa_status launch_seal(const CtxDev& c, int pending, cudaStream_t stream, bool pd
 // entry table_blocks = the open tail (sa_audit.cu).
 sa_status launch_audit(const CtxDev& c, const float* query, float* mass, float scale,
                        cudaStream_t stream);
+// History-prediction slot correction (sa_slots.cu); see sa_ctx_slot_correct.
+sa_status launch_slot_correct(const int32_t* selected, const int32_t* counts, int32_t* slots,
+                              int32_t* misses, int32_t* replace, int32_t* stats, int units,
+                              int budget, int id_limit, uint32_t* status, cudaStream_t stream);
 sa_status launch_pack_kv(uint16_t* packed, const float* key, const float* value,
                          size_t token, size_t elements, cudaStream_t stream);
 sa_status launch_xor(const uint8_t* in, uint8_t* out, size_t bytes, uint8_t mask,

@@ -423,3 +423,37 @@ def test_step_host_matches_device_step_pinned_and_pageable(pkg, cuda):
     assert (ref.generation.cpu().numpy() == 1).all()  # the 32nd append sealed
     for c, _ in ctxs:
         c.close()
+
+
+def test_slot_table_follows_the_selection_bit_exact(pkg, port, cuda):
+    """sa_ctx_slot_correct over a decode loop: a resident window that starts
+    empty and follows each step's selection equals the oracle's
+    compare_prediction restatement bit for bit (slots, misses, replacement
+    slots, hit/miss counts)."""
+    import dataclasses
+
+    from solidattention_repro_b200 import workloads
+
+    w = dataclasses.replace(workloads.CONFIGS["cfg2"], name="slots-test", layers=2,
+                            context_blocks=96, budget_blocks=24, hot_blocks=4)
+    ctx, info = workloads.make_context(w, 40, cuda, seed=8)
+    q, kv = workloads.decode_inputs(w, info, 36, cuda, seed=8)
+    slots = ctx.new_slots()
+    ref = slots.cpu().numpy().reshape(-1, w.budget_blocks)
+    total_hits = 0
+    for s in range(36):
+        ctx.step(q[s], kv[s])
+        misses, replace, stats = ctx.slot_correct(slots)
+        ctx.sync()
+        sel = ctx.selected.cpu().numpy().reshape(-1, w.budget_blocks)
+        cnt = ctx.selected_count.cpu().numpy().reshape(-1)
+        ref, mi, re, st = port.slot_correct(sel, cnt, ref)
+        assert np.array_equal(slots.cpu().numpy().reshape(ref.shape), ref), s
+        assert np.array_equal(misses.cpu().numpy().reshape(mi.shape), mi), s
+        assert np.array_equal(replace.cpu().numpy().reshape(re.shape), re), s
+        assert np.array_equal(stats.cpu().numpy().reshape(st.shape), st), s
+        if s > 0:
+            total_hits += int(st[:, 0].sum())
+    assert total_hits > 0  # consecutive selections overlap (the forced blocks at least)
+    assert ctx.status_bits() == 0
+    ctx.close()

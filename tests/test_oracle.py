@@ -223,3 +223,62 @@ def test_cpu_step_port_equals_reference(port, ref):
     a = port.sparse_step(pool, table, reps, q, tails, 9, qh, kh, 128, 32, nb, 6, 1, 2, cases.SCALE, 2)
     b = ref.sparse_step(pool, table, reps, q, tails, 9, qh, kh, 128, 32, nb, 6, 1, 2, cases.SCALE, 2)
     assert np.array_equal(a[0], b[0]) and np.array_equal(bits(a[1]), bits(b[1]))
+
+
+def _compare_prediction(predicted, oracle):
+    """cpp/src/pipeline_main.cpp:686-717, transliterated: hits, misses (oracle
+    order), replacement slots (slot order), and the corrected resident set."""
+    evicted = [s for s, b in enumerate(predicted) if b not in oracle]
+    misses = [b for b in oracle if b not in predicted]
+    assert len(misses) == len(evicted)  # the reference throws otherwise
+    corrected = list(predicted)
+    for m, s in zip(misses, evicted):
+        corrected[s] = m
+    assert sorted(corrected) == list(oracle)
+    return len(predicted) - len(evicted), misses, evicted, corrected
+
+
+def test_slot_correct_matches_compare_prediction(port):
+    """The oracle's slot correction equals the reference's compare_prediction
+    on full windows (both sets `budget` distinct blocks)."""
+    rng = np.random.default_rng(21)
+    budget, nb = 16, 60
+    sel, cnt, slots, want = [], [], [], []
+    for _ in range(200):
+        predicted = rng.choice(nb, budget, replace=False).tolist()
+        overlap = rng.integers(0, budget + 1)
+        keep = rng.choice(predicted, overlap, replace=False).tolist()
+        rest = [b for b in rng.permutation(nb).tolist() if b not in predicted][:budget - overlap]
+        oracle = sorted(keep + rest)
+        want.append(_compare_prediction(predicted, oracle))
+        sel.append(oracle)
+        cnt.append(budget)
+        slots.append(predicted)
+    got_slots, mi, re, st = port.slot_correct(np.array(sel), np.array(cnt), np.array(slots))
+    for u, (hits, misses, evicted, corrected) in enumerate(want):
+        assert st[u].tolist() == [hits, len(misses)]
+        assert mi[u, :len(misses)].tolist() == misses and (mi[u, len(misses):] == -1).all()
+        assert re[u, :len(evicted)].tolist() == evicted and (re[u, len(evicted):] == -1).all()
+        assert got_slots[u].tolist() == corrected
+
+
+def test_slot_correct_empty_slots_and_short_selections(port):
+    """Generalisation beyond the reference's equal counts: empty slots are
+    always overwritten and slots freed beyond the misses are emptied, so the
+    corrected window holds exactly the selection; hits never move."""
+    rng = np.random.default_rng(22)
+    budget, nb = 12, 40
+    for _ in range(300):
+        count = int(rng.integers(0, budget + 1))
+        sel = np.full(budget, -1, np.int32)
+        sel[:count] = np.sort(rng.choice(nb, count, replace=False))
+        slots = rng.choice(nb, budget, replace=False).astype(np.int32)
+        slots[rng.random(budget) < 0.3] = -1
+        got, mi, re, st = port.slot_correct(sel[None], np.array([count]), slots[None])
+        got, mi, re = got[0], mi[0], re[0]
+        assert sorted(b for b in got if b >= 0) == sel[:count].tolist()
+        hits = [s for s in range(budget) if slots[s] >= 0 and slots[s] in sel[:count]]
+        assert all(got[s] == slots[s] for s in hits) and st[0, 0] == len(hits)
+        n_miss = count - len(hits)
+        assert st[0, 1] == n_miss and (mi[n_miss:] == -1).all() and (re[n_miss:] == -1).all()
+        assert all(got[re[k]] == mi[k] for k in range(n_miss))
