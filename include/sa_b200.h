@@ -340,6 +340,20 @@ SA_API sa_status sa_ctx_audit(sa_ctx* ctx, const float* query, float* mass_out);
  * Asynchronous on the context stream. */
 SA_API sa_status sa_ctx_slot_correct(sa_ctx* ctx, int32_t* slots, int32_t* misses,
                                      int32_t* replace, int32_t* stats);
+/* Blocks in the reference's main-store format (the rows the reference
+ * pwrites per sealed block, cpp/src/kv_lifecycle_main.cpp:104-108, and the
+ * layer segments of src/solidattention_lab/qwen_kv_lab.py:77-107): a block is
+ * [32 tokens][2 (K,V)][KH][D] FP16, 128 KiB at KH = 8. These copy logical
+ * blocks [first, first+count) of (seq, layer) -- through the block table --
+ * between the head-major pool and `store` [count][32][2][KH][D], which may be
+ * device memory or pinned, mapped host memory (a host tier's staging
+ * buffer); 16-byte aligned. Import fills blocks already in the table (after
+ * sa_ctx_prefill, or sealed ones being reloaded). Asynchronous on the
+ * context stream. */
+SA_API sa_status sa_ctx_import_blocks(sa_ctx* ctx, int32_t seq, int32_t layer, int32_t first,
+                                      int32_t count, const void* store);
+SA_API sa_status sa_ctx_export_blocks(sa_ctx* ctx, int32_t seq, int32_t layer, int32_t first,
+                                      int32_t count, void* store);
 
 /* ---- KV-head-sharded contexts: outputs gathered over peer memory ---------
  * No reference counterpart as a function: replaces the all-gather of

@@ -380,6 +380,27 @@ class DecodeContext:
                                      mass.data_ptr()), "sa_ctx_audit")
         return mass
 
+    def import_blocks(self, seq: int, layer: int, first: int, store: torch.Tensor) -> None:
+        """Fill logical blocks [first, first + n) of (seq, layer) from store rows
+        [n, 32, 2, KH, 128] FP16 (device or pinned host; sa_ctx_import_blocks)."""
+        if store.dtype != torch.float16 or store.dim() != 5 or store.shape[1:] != (
+                BLOCK_TOKENS, 2, self.kh, HEAD_DIM) or not store.is_contiguous():
+            raise ValueError("store must be contiguous float16 [n, 32, 2, KH, 128]")
+        check(self._lib.sa_ctx_import_blocks(self._h, seq, layer, first, store.shape[0],
+                                             store.data_ptr()), "sa_ctx_import_blocks")
+
+    def export_blocks(self, seq: int, layer: int, first: int, count: int,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+        """Logical blocks [first, first + count) of (seq, layer) as store rows
+        [count, 32, 2, KH, 128] FP16 (sa_ctx_export_blocks); `out` may be a
+        pinned host tensor."""
+        if out is None:
+            out = torch.empty(count, BLOCK_TOKENS, 2, self.kh, HEAD_DIM, dtype=torch.float16,
+                              device=self.device)
+        check(self._lib.sa_ctx_export_blocks(self._h, seq, layer, first, count, out.data_ptr()),
+              "sa_ctx_export_blocks")
+        return out
+
     def new_slots(self) -> torch.Tensor:
         """An empty slot table [S*L, groups, budget] (-1) for slot_correct."""
         return torch.full((self.num_sl, self.n_groups, self.budget), -1, dtype=torch.int32,

@@ -107,6 +107,8 @@ PROTOTYPES = {
     "sa_ctx_launch_count": (C.c_uint64, [_vp]),
     "sa_ctx_audit": (C.c_int, [_vp, _vp, _vp]),
     "sa_ctx_slot_correct": (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
+    "sa_ctx_import_blocks": (C.c_int, [_vp, _i32, _i32, _i32, _i32, _vp]),
+    "sa_ctx_export_blocks": (C.c_int, [_vp, _i32, _i32, _i32, _i32, _vp]),
     "sa_ctx_gather_buffer": (C.c_int, [_vp, _i32, C.POINTER(_vp), C.POINTER(_sz)]),
     "sa_ctx_gather_attach": (C.c_int, [_vp, _i32, C.POINTER(_vp)]),
     "sa_ctx_gather_wait": (C.c_int, [_vp, C.POINTER(_vp)]),

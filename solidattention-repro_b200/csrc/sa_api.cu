@@ -1083,6 +1083,49 @@ SA_API sa_status sa_ctx_slot_correct(sa_ctx* c, int32_t* slots, int32_t* misses,
                              c->cfg.table_blocks, c->dev.status, c->stream);
 }
 
+namespace {
+sa_status ctx_store_blocks(sa_ctx* c, int32_t seq, int32_t layer, int32_t first, int32_t count,
+                           void* store, bool import) {
+  if (!c || !store) return fail(SA_ERR_INVALID_ARG, "blocks: null argument");
+  if (seq < 0 || seq >= c->cfg.seqs || layer < 0 || layer >= c->cfg.layers)
+    return fail(SA_ERR_INVALID_ARG, "blocks: sequence or layer out of range");
+  if (first < 0 || count < 0 || first + count > c->cfg.table_blocks)
+    return fail(SA_ERR_INVALID_ARG, "blocks: logical range beyond the block table");
+  DeviceGuard guard(c->cfg.device);
+  // the kernel touches `store` directly: it must be this device's memory or
+  // pinned host memory mapped for the device (never pageable memory)
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, store) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(SA_ERR_INVALID_ARG, "blocks: store is not device or pinned host memory");
+  }
+  void* dev = nullptr;
+  if ((a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) &&
+      a.device == c->cfg.device)
+    dev = store;
+  else if (a.type == cudaMemoryTypeHost && a.devicePointer)
+    dev = a.devicePointer;
+  if (!dev)
+    return fail(SA_ERR_INVALID_ARG,
+                "blocks: store must be memory of the context's device or pinned, mapped host memory");
+  if (reinterpret_cast<uintptr_t>(dev) & 15u)
+    return fail(SA_ERR_INVALID_ARG, "blocks: store buffer must be 16-byte aligned");
+  ++c->launches;
+  return launch_store_blocks(c->dev, seq * c->cfg.layers + layer, first, count, dev, import,
+                             c->stream);
+}
+}  // namespace
+
+SA_API sa_status sa_ctx_import_blocks(sa_ctx* c, int32_t seq, int32_t layer, int32_t first,
+                                      int32_t count, const void* store) {
+  return ctx_store_blocks(c, seq, layer, first, count, const_cast<void*>(store), true);
+}
+
+SA_API sa_status sa_ctx_export_blocks(sa_ctx* c, int32_t seq, int32_t layer, int32_t first,
+                                      int32_t count, void* store) {
+  return ctx_store_blocks(c, seq, layer, first, count, store, false);
+}
+
 // ------------------------------------------- KV-head-sharded gather over peer memory
 
 SA_API sa_status sa_ctx_gather_buffer(sa_ctx* c, int32_t world, void** buf_out,

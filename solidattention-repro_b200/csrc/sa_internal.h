@@ -224,6 +224,10 @@ sa_status launch_audit(const CtxDev& c, const float* query, float* mass, float s
 sa_status launch_slot_correct(const int32_t* selected, const int32_t* counts, int32_t* slots,
                               int32_t* misses, int32_t* replace, int32_t* stats, int units,
                               int budget, int id_limit, uint32_t* status, cudaStream_t stream);
+// Copy sealed blocks [first, first+count) of sequence-layer sl between the
+// head-major pool and store rows [count][32][2][KH][128] (sa_lifecycle.cu).
+sa_status launch_store_blocks(const CtxDev& c, int sl, int first, int count, void* store,
+                              bool import, cudaStream_t stream);
 sa_status launch_pack_kv(uint16_t* packed, const float* key, const float* value,
                          size_t token, size_t elements, cudaStream_t stream);
 sa_status launch_xor(const uint8_t* in, uint8_t* out, size_t bytes, uint8_t mask,

@@ -444,3 +444,54 @@ sa_status launch_consume(const float* out, int n, float* checksum, cudaStream_t 
 }
 
 }  // namespace sa
+
+namespace sa {
+
+namespace {
+
+// grid (count, kv_heads): one (block, KV head) = 16 KB per CTA. Token-major
+// store rows [32][2][KH][128] <-> the head-major pool's [KH][2][32][128].
+template <bool kImport>
+__global__ void __launch_bounds__(256)
+    store_blocks_kernel(const CtxDev c, int sl, int first, uint16_t* store) {
+  const int b = blockIdx.x, h = blockIdx.y;
+  const int logical = first + b;
+  if (logical < 0 || logical >= c.table_blocks) {
+    if (threadIdx.x == 0) raise_status(c.status, SA_DEV_BAD_BLOCK);
+    return;
+  }
+  const int phys = c.table[(int64_t)sl * c.table_blocks + logical];
+  if (phys < 0 || phys >= c.pool_blocks) {
+    if (threadIdx.x == 0) raise_status(c.status, SA_DEV_BAD_BLOCK);
+    return;
+  }
+  uint16_t* pool = c.pool + ((int64_t)phys * c.kv_heads + h) * 2 * kBlockTokens * kHeadDim;
+  uint16_t* rows = store + (int64_t)b * kBlockTokens * c.row_elems;
+  constexpr int kChunks = 2 * kBlockTokens * kHeadDim / 8;  // 16-byte chunks of the (block, head)
+  for (int i = threadIdx.x; i < kChunks; i += blockDim.x) {
+    const int kv = i / (kBlockTokens * kHeadDim / 8);
+    const int t = (i / (kHeadDim / 8)) % kBlockTokens;
+    const int d = (i % (kHeadDim / 8)) * 8;
+    uint4* p = reinterpret_cast<uint4*>(pool + ((int64_t)kv * kBlockTokens + t) * kHeadDim + d);
+    uint4* r = reinterpret_cast<uint4*>(rows + ((int64_t)t * 2 + kv) * c.kv_heads * kHeadDim +
+                                        (int64_t)h * kHeadDim + d);
+    if (kImport) *p = *r;
+    else *r = *p;
+  }
+}
+
+}  // namespace
+
+sa_status launch_store_blocks(const CtxDev& c, int sl, int first, int count, void* store,
+                              bool import, cudaStream_t stream) {
+  if (count <= 0) return SA_OK;
+  if (count > 65535) return fail(SA_ERR_UNSUPPORTED, "blocks: more than 65535 blocks per call");
+  const dim3 grid(count, c.kv_heads);
+  if (import)
+    store_blocks_kernel<true><<<grid, 256, 0, stream>>>(c, sl, first, static_cast<uint16_t*>(store));
+  else
+    store_blocks_kernel<false><<<grid, 256, 0, stream>>>(c, sl, first, static_cast<uint16_t*>(store));
+  return cuda_status(cudaGetLastError(), "store_blocks_kernel launch");
+}
+
+}  // namespace sa

@@ -457,3 +457,37 @@ def test_slot_table_follows_the_selection_bit_exact(pkg, port, cuda):
     assert total_hits > 0  # consecutive selections overlap (the forced blocks at least)
     assert ctx.status_bits() == 0
     ctx.close()
+
+
+def test_store_blocks_round_trip_reference_format(pkg, cuda):
+    """sa_ctx_import_blocks / sa_ctx_export_blocks: logical blocks move between
+    the head-major pool and the reference's store rows [32][2][KH][128], from
+    device memory and from pinned host memory, equal to the token-major
+    conversion of the pool; pageable host memory is refused, not touched."""
+    qh, kh, nb = 8, 4, 12
+    ctx = pkg.DecodeContext(query_heads=qh, kv_heads=kh, layers=2, seqs=2,
+                            pool_blocks=4 * (nb + 2), table_blocks=nb + 1, budget_blocks=4,
+                            init_blocks=1, local_blocks=1, device=cuda)
+    g = torch.Generator().manual_seed(9)
+    for s in range(2):
+        for l in range(2):
+            ctx.prefill(s, l, nb)
+    store = torch.randn(nb, 32, 2, kh, D, generator=g).half()
+    ctx.import_blocks(1, 0, 0, store.to(cuda))                  # from device memory
+    pinned = torch.randn(5, 32, 2, kh, D, generator=g).half().pin_memory()
+    ctx.import_blocks(1, 1, 3, pinned)                          # from pinned host memory
+    ctx.sync()
+    table = ctx.table.cpu().numpy()
+    assert torch.equal(ctx.read_blocks(table[2, :nb]).cpu(), store)
+    assert torch.equal(ctx.read_blocks(table[3, 3:8]).cpu(), pinned)
+    assert torch.equal(ctx.export_blocks(1, 0, 0, nb).cpu(), store)
+    host = torch.empty(5, 32, 2, kh, D, dtype=torch.float16).pin_memory()
+    ctx.export_blocks(1, 1, 3, 5, host)
+    ctx.sync()
+    assert torch.equal(host, pinned)
+    with pytest.raises(pkg.SparseKVError):
+        ctx.import_blocks(0, 0, 0, torch.zeros(1, 32, 2, kh, D, dtype=torch.float16))  # pageable
+    with pytest.raises(pkg.SparseKVError):
+        ctx.export_blocks(0, 0, nb, 2)  # beyond the table
+    assert ctx.status_bits() == 0
+    ctx.close()
