@@ -296,6 +296,20 @@ SA_API sa_status sa_ctx_build_reps(sa_ctx* ctx, int32_t seq, int32_t layer,
  *   out [seqs][layers][QH][D] (FP16 or FP32 per config). */
 SA_API sa_status sa_ctx_step(sa_ctx* ctx, const float* query,
                              const void* kv_new, int32_t kv_fp32, void* out);
+/* The decode step from raw projections, with the append fused with its
+ * producers (head_rms + rope + append_fp16_kv, cpp/src/qwen_layer_main.cpp:
+ * 146-183, 270-281, in the order of cpp/src/qwen_chain_main.cpp:370-392):
+ * queries and keys are RMS-normalised per head with the layer's q_norm /
+ * k_norm weights and rotated (rotate-half RoPE at the sequence's position),
+ * then the keys and values are packed to FP16 into the tail.
+ *   q_raw [seqs][layers][QH][D], k_raw and v [seqs][layers][KH][D] FP32;
+ *   q_norm_w, k_norm_w [layers][D] FP32; positions [seqs] int32 (decode
+ *   position of this token); all device pointers; out as in sa_ctx_step.
+ * head_dim 128 only. */
+SA_API sa_status sa_ctx_step_raw(sa_ctx* ctx, const float* q_raw, const float* k_raw,
+                                 const float* v, const float* q_norm_w, const float* k_norm_w,
+                                 const int32_t* positions, float rope_theta, float norm_eps,
+                                 void* out);
 /* The same step from host buffers: H2D inputs, step, D2H output, synchronize
  * (the end-to-end call of a host-side decode loop). */
 SA_API sa_status sa_ctx_step_host(sa_ctx* ctx, const float* query_host,

@@ -211,6 +211,17 @@ class Port(_Lib):
         o = np.ascontiguousarray(offsets, np.int64).reshape(-1)
         return int(self.lib.sao_fnv_offsets(o, o.size))
 
+    def head_norm_rope(self, rows, weight, position, theta, eps):
+        """Rows [..., 128] FP32 normalised and rotated (see sao_head_norm_rope)."""
+        r = np.array(rows, np.float32, copy=True)
+        w = np.ascontiguousarray(weight, np.float32)
+        P = C.c_void_p
+        self.lib.sao_head_norm_rope.argtypes = [P, _sz, P, C.c_int, C.c_float, C.c_float]
+        self.lib.sao_head_norm_rope.restype = None
+        self.lib.sao_head_norm_rope(r.ctypes.data, r.size // 128, w.ctypes.data, int(position),
+                                    float(theta), float(eps))
+        return r
+
     def slot_correct(self, selected, counts, slots):
         """compare_prediction per unit (see sao_slot_correct): returns the
         corrected slots, misses, replacement slots and (hits, misses)."""

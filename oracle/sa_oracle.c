@@ -567,3 +567,29 @@ void sao_slot_correct(const int32_t* selected, const int32_t* counts, int32_t* s
     free(freed);
   }
 }
+
+/* head_rms (cpp/src/qwen_layer_main.cpp:146-161): squares reduced pairwise
+ * with strides 64, 32, ..., 1 as its 128 threads do, then value *
+ * rsqrt(mean + eps) * weight (the reference's device rsqrtf; 1 / sqrtf here).
+ * rope (:163-183): dim d pairs with d +- 64, frequency theta^(-2 i / 128),
+ * angle = position * frequency, rotate-half. */
+void sao_head_norm_rope(float* rows, size_t nrows, const float* weight, int position,
+                        float theta, float eps) {
+  float red[128], x[128];
+  for (size_t r = 0; r < nrows; ++r) {
+    float* v = rows + r * 128;
+    for (int t = 0; t < 128; ++t) red[t] = v[t] * v[t];
+    for (int stride = 64; stride > 0; stride >>= 1)
+      for (int t = 0; t < stride; ++t) red[t] += red[t + stride];
+    const float inv = 1.0f / sqrtf(red[0] / 128.0f + eps);
+    for (int t = 0; t < 128; ++t) x[t] = v[t] * inv * weight[t];
+    for (int t = 0; t < 128; ++t) {
+      const int paired = t < 64 ? t + 64 : t - 64;
+      const int fi = t < 64 ? t : t - 64;
+      const float freq = powf(theta, -2.0f * (float)fi / 128.0f);
+      const float angle = (float)position * freq;
+      const float rotated = t < 64 ? -x[paired] : x[paired];
+      v[t] = x[t] * cosf(angle) + rotated * sinf(angle);
+    }
+  }
+}

@@ -22,6 +22,7 @@
  *                              cpp/src/qwen_chain_main.cpp:360-395 (token order)
  *   sao_lifecycle_run          cpp/src/kv_lifecycle_main.cpp:25-113
  *   sao_slot_correct           cpp/src/pipeline_main.cpp:686-717
+ *   sao_head_norm_rope         cpp/src/qwen_layer_main.cpp:146-183
  *
  * Parity of this restatement is pinned against the reference compiled from
  * its own sources (oracle/_ref) and against the reference's published known
@@ -146,6 +147,12 @@ void sao_top4_first_max(const float* scores, size_t block_tokens, int64_t* out);
 void sao_slot_correct(const int32_t* selected, const int32_t* counts, int32_t* slots,
                       int32_t* misses, int32_t* replace, int32_t* stats, size_t units,
                       size_t budget);
+
+/* Per-head RMS norm then rotate-half RoPE on rows of 128 floats, in place:
+ * head_rms (cpp/src/qwen_layer_main.cpp:146-161, pairwise sum of squares,
+ * strides 64..1) and rope (:163-183) at one position. */
+void sao_head_norm_rope(float* rows, size_t nrows, const float* weight, int position,
+                        float theta, float eps);
 
 /* FNV-1a over 64-bit words, as the C2.1 driver hashes representative offsets
  * (cpp/src/selection_main.cpp:167-171). */

@@ -335,6 +335,21 @@ class DecodeContext:
         check(self._lib.sa_ctx_step(self._h, q, kv, f32, out.data_ptr()), "sa_ctx_step")
         return out
 
+    def step_raw(self, q_raw: torch.Tensor, k_raw: torch.Tensor, v: torch.Tensor,
+                 q_norm_w: torch.Tensor, k_norm_w: torch.Tensor, positions: torch.Tensor,
+                 rope_theta: float = 1.0e6, norm_eps: float = 1e-6,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+        """Decode step from raw projections (q/k norm + RoPE + FP16 pack fused
+        with the append; sa_ctx_step_raw). q_raw [S, L, QH, 128], k_raw and v
+        [S, L, KH, 128] FP32; q_norm_w, k_norm_w [L, 128]; positions [S] int32."""
+        out = self.new_output() if out is None else out
+        check(self._lib.sa_ctx_step_raw(
+            self._h, _dev_ptr(q_raw, torch.float32, "q_raw"), _dev_ptr(k_raw, torch.float32, "k_raw"),
+            _dev_ptr(v, torch.float32, "v"), _dev_ptr(q_norm_w, torch.float32, "q_norm_w"),
+            _dev_ptr(k_norm_w, torch.float32, "k_norm_w"), _dev_ptr(positions, torch.int32, "positions"),
+            float(rope_theta), float(norm_eps), out.data_ptr()), "sa_ctx_step_raw")
+        return out
+
     def step_host(self, query: np.ndarray | torch.Tensor, kv_new: np.ndarray | torch.Tensor,
                   out: np.ndarray | torch.Tensor, kv_fp32: bool = False) -> None:
         """End-to-end step from host buffers (H2D, step, D2H, synchronize)."""

@@ -107,6 +107,7 @@ PROTOTYPES = {
     "sa_ctx_launch_count": (C.c_uint64, [_vp]),
     "sa_ctx_audit": (C.c_int, [_vp, _vp, _vp]),
     "sa_ctx_slot_correct": (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
+    "sa_ctx_step_raw": (C.c_int, [_vp] * 7 + [C.c_float, C.c_float, _vp]),
     "sa_ctx_import_blocks": (C.c_int, [_vp, _i32, _i32, _i32, _i32, _vp]),
     "sa_ctx_export_blocks": (C.c_int, [_vp, _i32, _i32, _i32, _i32, _vp]),
     "sa_ctx_gather_buffer": (C.c_int, [_vp, _i32, C.POINTER(_vp), C.POINTER(_sz)]),

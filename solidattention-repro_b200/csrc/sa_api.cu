@@ -140,6 +140,7 @@ struct sa_ctx {
   AttnPlan attn_plan{};
   // staging for sa_ctx_step_host
   float* d_query = nullptr;
+  float* d_qt = nullptr;  // normalised, rotated queries of sa_ctx_step_raw
   void* d_kv_new = nullptr;
   void* d_out = nullptr;
   uint32_t* h_status = nullptr;  // pinned
@@ -626,10 +627,8 @@ sa_status dalloc(T** p, size_t count) {
 }
 
 // kv_new non-null: the select kernel also appends the step's token (fused).
-sa_status ctx_select(sa_ctx* c, const float* query, const void* kv_new = nullptr,
-                     int kv_fp32 = 0, bool pdl = false) {
+SelectParams select_params(sa_ctx* c, const float* query) {
   SelectParams p{};
-  p.pdl = pdl;
   p.query = query;
   p.reps = c->dev.reps;
   p.s_dim = c->table_pad;
@@ -652,6 +651,13 @@ sa_status ctx_select(sa_ctx* c, const float* query, const void* kv_new = nullptr
   p.scores = c->scores;
   p.counters = c->select_counters;
   p.status = c->dev.status;
+  return p;
+}
+
+sa_status ctx_select(sa_ctx* c, const float* query, const void* kv_new = nullptr,
+                     int kv_fp32 = 0, bool pdl = false) {
+  SelectParams p = select_params(c, query);
+  p.pdl = pdl;
   if (kv_new) {
     p.append_ctx = c->dev;
     p.append_kv = kv_new;
@@ -766,6 +772,7 @@ SA_API sa_status sa_ctx_create(const sa_ctx_config* config, sa_ctx** out) {
                 attention_scratch_bytes(c->attn_plan, units, c->group));
   if (st == SA_OK) st = dalloc(&c->attn_counters, (size_t)units);
   if (st == SA_OK) st = dalloc(&c->d_query, nsl * g.query_heads * kHeadDim);
+  if (st == SA_OK) st = dalloc(&c->d_qt, nsl * g.query_heads * kHeadDim);
   if (st == SA_OK) st = dalloc(reinterpret_cast<float**>(&c->d_kv_new), nsl * row_elems);
   if (st == SA_OK) st = dalloc(reinterpret_cast<float**>(&c->d_out), nsl * g.query_heads * kHeadDim);
   if (st == SA_OK)
@@ -805,7 +812,7 @@ SA_API sa_status sa_ctx_destroy(sa_ctx* c) {
   void* ptrs[] = {d.pool, d.reps, d.table, d.num_sealed, d.tail_block, d.tail_len, d.generation,
                   d.query_ring, d.free_list, d.free_top, d.seal_counters, d.status, c->selected,
                   c->selected_count, c->scores, c->select_counters, c->attn_partial,
-                  c->attn_counters, c->d_query, c->d_kv_new, c->d_out, c->gather_buf,
+                  c->attn_counters, c->d_query, c->d_qt, c->d_kv_new, c->d_out, c->gather_buf,
                   c->gather_peers};
   for (void* p : ptrs) cudaFree(p);
   if (c->h_status) cudaFreeHost(c->h_status);
@@ -1081,6 +1088,34 @@ SA_API sa_status sa_ctx_slot_correct(sa_ctx* c, int32_t* slots, int32_t* misses,
   return launch_slot_correct(c->selected, c->selected_count, slots, misses, replace, stats,
                              c->num_sl * c->n_sel_groups, c->cfg.budget_blocks,
                              c->cfg.table_blocks, c->dev.status, c->stream);
+}
+
+SA_API sa_status sa_ctx_step_raw(sa_ctx* c, const float* q_raw, const float* k_raw,
+                                 const float* v, const float* q_norm_w, const float* k_norm_w,
+                                 const int32_t* positions, float rope_theta, float norm_eps,
+                                 void* out) {
+  if (!c || !q_raw || !k_raw || !v || !q_norm_w || !k_norm_w || !positions || !out)
+    return fail(SA_ERR_INVALID_ARG, "step_raw: null argument");
+  if (!(rope_theta > 0.f) || !(norm_eps >= 0.f))
+    return fail(SA_ERR_INVALID_ARG, "step_raw: bad rope theta or norm epsilon");
+  DeviceGuard guard(c->cfg.device);
+  SelectParams p = select_params(c, q_raw);
+  p.append_ctx = c->dev;
+  p.raw_k = k_raw;
+  p.raw_v = v;
+  p.q_norm_w = q_norm_w;
+  p.k_norm_w = k_norm_w;
+  p.positions = positions;
+  p.raw_qt = c->d_qt;
+  p.layers = c->cfg.layers;
+  p.rope_theta = rope_theta;
+  p.norm_eps = norm_eps;
+  ++c->launches;
+  sa_status st = launch_select(p, c->stream);
+  if (st != SA_OK) return st;
+  if ((st = ctx_attend(c, c->d_qt, out, 1, true)) != SA_OK) return st;
+  ++c->launches;
+  return launch_seal(c->dev, 1, c->stream, true);
 }
 
 namespace {

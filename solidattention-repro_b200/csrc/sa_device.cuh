@@ -176,6 +176,37 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 // programmatic-serialization attribute.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// ---- per-head RMS norm + rotary embedding (Qwen3 q/k norm) --------------------
+
+// One 128-wide head row held in shared memory `row`, transformed in place by
+// the 128 threads of a CTA (thread t owns element t): RMS norm with the
+// reference's pairwise reduction order (head_rms, cpp/src/qwen_layer_main.cpp:
+// 146-161: square, then strides 64, 32, ..., 1), then rotate-half RoPE at
+// `position` (rope, :163-183). `red` is 128 floats of scratch. Both must be
+// called by all 128 threads.
+__device__ __forceinline__ void head_norm_rope(float* row, float* red, const float* weight,
+                                               int position, float theta, float eps, int t) {
+  const float v = row[t];
+  red[t] = v * v;
+  __syncthreads();
+  for (int stride = 64; stride > 0; stride >>= 1) {
+    if (t < stride) red[t] += red[t + stride];
+    __syncthreads();
+  }
+  row[t] = v * rsqrtf(red[0] / 128.0f + eps) * weight[t];
+  __syncthreads();
+  const int half = 64;
+  const int paired = t < half ? t + half : t - half;
+  const int fi = t < half ? t : t - half;
+  const float freq = powf(theta, -2.0f * fi / 128.0f);
+  const float angle = position * freq;
+  const float x = row[t];
+  const float rotated = t < half ? -row[paired] : row[paired];
+  __syncthreads();
+  row[t] = x * cosf(angle) + rotated * sinf(angle);
+  __syncthreads();
+}
+
 // ---- decode-tail append ------------------------------------------------------
 
 // Writes the step's K/V of KV heads [kvh0, kvh1) of sequence-layer sl into

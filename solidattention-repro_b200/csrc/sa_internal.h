@@ -172,6 +172,19 @@ struct SelectParams {
   CtxDev append_ctx;
   const void* append_kv;  // [num_sl][2][kv_heads][128] FP16, or FP32 when append_kv_fp32
   int append_kv_fp32;
+  // Raw projections (raw_k null = off): `query` holds pre-norm queries; every
+  // CTA normalises and rotates its group's rows as it loads them, and the
+  // first CTA of a unit writes them to raw_qt (for the attention) and the
+  // query ring, and appends the normalised, rotated K (raw_k) and V (raw_v)
+  // [num_sl][kv_heads][128] FP32 of its KV heads packed to FP16.
+  const float* raw_k;
+  const float* raw_v;
+  const float* q_norm_w;   // [layers][128]
+  const float* k_norm_w;   // [layers][128]
+  const int32_t* positions;  // [num_sl / layers]
+  float* raw_qt;           // [num_sl][qh][128]
+  int layers;
+  float rope_theta, norm_eps;
   int pdl;  // launched as a programmatic dependent of the previous kernel
 };
 

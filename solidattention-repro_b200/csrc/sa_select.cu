@@ -102,6 +102,52 @@ __device__ __forceinline__ void head_dots(const SelectParams& p, const float* rh
   }
 }
 
+// Raw projections (Qwen3 decode: q_norm / k_norm, then RoPE, then the FP16
+// pack -- head_rms, rope and append_fp16_kv of cpp/src/qwen_layer_main.cpp,
+// in the order of cpp/src/qwen_chain_main.cpp:370-392): normalise and rotate
+// the group's query rows in qs; the unit's first CTA also publishes them
+// (raw_qt for the attention, the query ring for the seal) and appends the
+// normalised, rotated K and the V of the group's KV heads to the tail row.
+// All 128 threads call it; `scratch` holds >= 256 floats.
+__device__ void raw_projections(const SelectParams& p, int sl, int g, float* qs, float* scratch) {
+  const int t = threadIdx.x;
+  const int layer = sl % p.layers;
+  const int pos = p.positions[sl / p.layers];
+  for (int j = 0; j < p.group; ++j)
+    head_norm_rope(qs + j * kHeadDim, scratch, p.q_norm_w + (size_t)layer * kHeadDim, pos,
+                   p.rope_theta, p.norm_eps, t);
+  if (blockIdx.x != 0) return;
+  const CtxDev& c = p.append_ctx;
+  const int q0 = g * p.group;
+  const int tl = c.tail_len[sl];
+  const int phys = c.tail_block[sl];
+  const bool ok_tail = tl >= 0 && tl < kBlockTokens;
+  const bool ok_block = phys >= 0 && phys < c.pool_blocks;
+  if (t == 0 && !ok_tail) raise_status(c.status, SA_DEV_TAIL_FULL);
+  if (t == 0 && ok_tail && !ok_block) raise_status(c.status, SA_DEV_BAD_BLOCK);
+  for (int j = 0; j < p.group; ++j) {
+    const float v = qs[j * kHeadDim + t];
+    p.raw_qt[((size_t)sl * p.qh + q0 + j) * kHeadDim + t] = v;
+    if (ok_tail && ok_block)
+      c.query_ring[(((size_t)sl * c.qh + q0 + j) * kBlockTokens + tl) * kHeadDim + t] = v;
+  }
+  if (!ok_tail || !ok_block) return;
+  const int per_kv = p.qh / c.kv_heads;
+  float* row = scratch;
+  float* red = scratch + kHeadDim;
+  for (int h = q0 / per_kv; h < (q0 + p.group) / per_kv; ++h) {
+    const size_t src = ((size_t)sl * c.kv_heads + h) * kHeadDim + t;
+    row[t] = p.raw_k[src];
+    __syncthreads();
+    head_norm_rope(row, red, p.k_norm_w + (size_t)layer * kHeadDim, pos, p.rope_theta,
+                   p.norm_eps, t);
+    uint16_t* block = c.pool + (((size_t)phys * c.kv_heads + h) * 2) * kBlockTokens * kHeadDim;
+    block[(size_t)tl * kHeadDim + t] = f2h_rn(row[t]);
+    block[((size_t)kBlockTokens + tl) * kHeadDim + t] = f2h_rn(p.raw_v[src]);
+    __syncthreads();
+  }
+}
+
 __global__ void __launch_bounds__(kThreads)
     select_kernel(const SelectParams p, const int vec) {
   // dynamic shared memory: q [group][d], head dots [group][chunk], then (last
@@ -132,6 +178,7 @@ __global__ void __launch_bounds__(kThreads)
   const float* qsrc = p.query + ((size_t)sl * p.qh + (size_t)g * p.group) * p.d;
   for (int i = threadIdx.x; i < p.group * p.d; i += kThreads) qs[i] = qsrc[i];
   __syncthreads();
+  if (p.raw_k) raw_projections(p, sl, g, qs, dots);
 
   // ---- per-head dot products: warp w takes head w % hp (+ hp, ...) of
   // sub-chunk w / hp ----

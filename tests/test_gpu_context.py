@@ -491,3 +491,63 @@ def test_store_blocks_round_trip_reference_format(pkg, cuda):
         ctx.export_blocks(0, 0, nb, 2)  # beyond the table
     assert ctx.status_bits() == 0
     ctx.close()
+
+
+def test_step_raw_fuses_qk_norm_rope_into_the_append(pkg, port, cuda):
+    """sa_ctx_step_raw (q/k norm + RoPE + FP16 pack fused with the append) equals
+    sa_ctx_step fed with the oracle's transformed queries and keys: the query
+    ring, the packed K (plus one FP16 ulp) and the attention output within
+    the float tolerance of CUDA's vs the C library's powf/cosf/sinf/rsqrt,
+    V exactly, and the selections identical."""
+    import dataclasses
+
+    from solidattention_repro_b200 import workloads
+
+    w = dataclasses.replace(workloads.CONFIGS["cfg3"], name="raw-test", layers=2, seqs=2,
+                            context_blocks=48, budget_blocks=12, hot_blocks=2)
+    raw, _ = workloads.make_context(w, 8, cuda, seed=5)
+    ref, _ = workloads.make_context(w, 8, cuda, seed=5)
+    rng = np.random.default_rng(12)
+    qw = (1 + 0.1 * rng.standard_normal((w.layers, 128))).astype(np.float32)
+    kw = (1 + 0.1 * rng.standard_normal((w.layers, 128))).astype(np.float32)
+    positions = np.array([48 * 32, 48 * 32 + 7000], np.int32)
+    theta, eps = 1.0e6, 1e-6
+    for step in range(3):
+        q = rng.standard_normal((w.seqs, w.layers, w.query_heads, 128), dtype=np.float32)
+        k = rng.standard_normal((w.seqs, w.layers, w.kv_heads, 128), dtype=np.float32)
+        v = rng.standard_normal((w.seqs, w.layers, w.kv_heads, 128), dtype=np.float32)
+        tl = raw.tail_len.cpu().numpy().copy()
+        tb = raw.tail_block.cpu().numpy().copy()
+        got = raw.step_raw(*(torch.from_numpy(a).to(cuda) for a in (q, k, v, qw, kw)),
+                           torch.from_numpy(positions + step).to(cuda), theta, eps)
+        qt, kt = q.copy(), k.copy()
+        for s in range(w.seqs):
+            for l in range(w.layers):
+                qt[s, l] = port.head_norm_rope(q[s, l], qw[l], positions[s] + step, theta, eps)
+                kt[s, l] = port.head_norm_rope(k[s, l], kw[l], positions[s] + step, theta, eps)
+        kv = np.stack([kt, v], 2).astype(np.float16)  # [S, L, 2, KH, 128]
+        want = ref.step(torch.from_numpy(qt).to(cuda), torch.from_numpy(kv).to(cuda))
+        ref.sync()
+        raw.sync()
+        g, wn = got.float().cpu().numpy(), want.float().cpu().numpy()
+        assert np.abs(g - wn).max() <= 2e-3 and cosine(g.ravel(), wn.ravel()) >= 0.99999, step
+        assert np.array_equal(raw.selected.cpu().numpy(), ref.selected.cpu().numpy()), step
+        ring = raw.query_ring.cpu().numpy()
+        pool = raw.pool.cpu().numpy()
+        for s in range(w.seqs):
+            for l in range(w.layers):
+                sl = s * w.layers + l
+                # an ulp of CUDA's vs the C library's powf moves the FP32 angle
+                # by ~1e-7 * position radians
+                tol = (1e-5 + 2e-7 * float(positions[s] + step)) * np.abs(qt[s, l]).max()
+                np.testing.assert_allclose(ring[sl, :, tl[sl]], qt[s, l], rtol=1e-5, atol=tol)
+                # the packed K: the same angle tolerance, plus one FP16 ulp
+                k16 = pool[tb[sl], :, 0, tl[sl]].astype(np.float32)
+                ktol = (1e-5 + 2e-7 * float(positions[s] + step)) * np.abs(kt[s, l]).max(1,
+                                                                                   keepdims=True)
+                ulp = np.abs(kt[s, l]) * 2.0 ** -10 + 2.0 ** -24
+                assert (np.abs(k16 - kt[s, l]) <= ktol + ulp).all()
+                assert np.array_equal(pool[tb[sl], :, 1, tl[sl]], v[s, l].astype(np.float16))
+    assert raw.status_bits() == 0
+    raw.close()
+    ref.close()

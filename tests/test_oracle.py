@@ -282,3 +282,25 @@ def test_slot_correct_empty_slots_and_short_selections(port):
         n_miss = count - len(hits)
         assert st[0, 1] == n_miss and (mi[n_miss:] == -1).all() and (re[n_miss:] == -1).all()
         assert all(got[re[k]] == mi[k] for k in range(n_miss))
+
+
+def test_head_norm_rope_matches_float64(port):
+    """The oracle's q/k norm + RoPE (head_rms + rope of qwen_layer_main.cpp)
+    against a float64 evaluation of the same formulas, with the angle
+    position * frequency formed in FP32 as the reference forms it (at
+    position 32767 that rounding alone moves the angle by ~2e-3 rad)."""
+    rng = np.random.default_rng(31)
+    rows = rng.standard_normal((6, 128), dtype=np.float32) * 3
+    w = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    for pos, theta in [(0, 1e6), (17, 1e6), (32767, 1e6), (4000, 1e4)]:
+        got = port.head_norm_rope(rows, w, pos, theta, 1e-6)
+        x = rows.astype(np.float64)
+        x = x / np.sqrt((x * x).mean(1, keepdims=True) + 1e-6) * w
+        i = np.arange(64, dtype=np.float32)
+        freq = np.power(np.float32(theta), np.float32(-2.0) * i / np.float32(128.0))
+        ang = (np.float32(pos) * freq.astype(np.float32)).astype(np.float64)
+        c, s = np.cos(ang), np.sin(ang)
+        want = np.concatenate([x[:, :64] * c - x[:, 64:] * s, x[:, 64:] * c + x[:, :64] * s], 1)
+        # powf / cosf / sinf of the C library may round an ulp off numpy's
+        np.testing.assert_allclose(got, want, rtol=1e-5,
+                                   atol=(1e-5 + 2e-7 * pos) * np.abs(want).max())
