@@ -31,10 +31,19 @@ _i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
 _sz = C.c_size_t
 
 
+# Where the reference project is checked out in the build container; the
+# environment variable SA_REFERENCE_ROOT overrides it. The GPU box has none.
+DEFAULT_REFERENCE_ROOT = "/root/reference"
+
+
+def reference_root_dir(reference_root: str | None = None) -> str:
+    return reference_root or os.environ.get("SA_REFERENCE_ROOT", DEFAULT_REFERENCE_ROOT)
+
+
 def build(reference_root: str | None = None) -> None:
     """Compile liboracle.so, and _ref/libsa_ref.so when the reference tree exists."""
     subprocess.run(["make", "-s", "-C", str(HERE), "all"], check=True)
-    ref = reference_root or os.environ.get("SA_REFERENCE_ROOT", "/root/reference")
+    ref = reference_root_dir(reference_root)
     if Path(ref, "cpp", "src", "selection.cpp").exists():
         subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={ref}"], check=True)
 

@@ -1,9 +1,10 @@
 """Generate the golden vectors under tests/golden/ from the reference itself.
 
-Run in a container that has the reference tree (default /root/reference) and
-the compiled reference (oracle/_ref, built by `python __graft_entry__.py build`):
+Run in a container that has the reference tree (its root given by --reference,
+else SA_REFERENCE_ROOT, else oracle.DEFAULT_REFERENCE_ROOT) and the compiled
+reference (oracle/_ref, built by `python __graft_entry__.py build`):
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py [--reference <reference root>]
 
 Outputs (small, committed; the GPU box has no reference tree):
 
@@ -100,13 +101,13 @@ def make_python_twins(reference: Path) -> dict:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=None)
     args = ap.parse_args()
     sys.path.insert(0, str(ROOT))
     sys.path.insert(0, str(HERE))
     import oracle
 
-    oracle.build(args.reference)
+    oracle.build(oracle.reference_root_dir(args.reference))
     ref = oracle.reference()
     if ref is None:
         raise SystemExit("oracle/_ref was not built: the reference tree is required")
