@@ -41,11 +41,19 @@ constexpr int kMaxBlocks = 16384;
 constexpr int kDimUnroll = 8;
 constexpr unsigned kFull = 0xffffffffu;
 
+constexpr int kTieMax = kThreads;  // threshold buckets this small are ranked directly
+
 struct TopkShared {
-  int hist[256];
-  int scan[33];
+  int hist[2][256];                 // radix histograms, double-buffered by pass
+  uint32_t tie_bits[kMaxBlocks / 32];   // chosen members of the threshold bucket
+  uint32_t pick_bits[kMaxBlocks / 32];  // chosen blocks, for the ordered compaction
+  uint32_t cand_key[kTieMax];       // threshold-bucket members gathered for ranking
+  int cand_idx[kTieMax];
   int digit;
   int above;
+  int bucket;
+  int ncand;
+  int warp_count[kWarps];
   int last;
 };
 
@@ -148,6 +156,198 @@ __device__ void raw_projections(const SelectParams& p, int sl, int g, float* qs,
   }
 }
 
+// Top-k of one unit over scores[0, nb), run by the unit's last CTA: the
+// forced blocks ([0, init) and the last `local`), then the K = budget -
+// |forced| unforced blocks that come first in (score descending, index
+// ascending) order -- the order of the reference's stable sort -- written
+// to ids in ascending index order.
+//
+// An MSB-first radix select over order-preserving 32-bit keys narrows the
+// threshold bucket (the blocks sharing the top bits of the K-th key) 8 bits
+// a pass. It stops as soon as the bucket is taken whole, or is small enough
+// (<= kTieMax blocks) to rank its members directly by (key, index); only a
+// bucket of more than kTieMax exactly equal keys is resolved by index order
+// over warp segments. Compaction runs over warp segments too: warp w covers
+// blocks [w * seg, (w + 1) * seg), seg a multiple of 32, one block per lane
+// per step, so a ballot keeps index order inside a warp and one exchange of
+// warp totals keeps it across warps.
+__device__ void select_top_k(const SelectParams& p, int unit, int nb, const float* scores,
+                             uint32_t* keys, TopkShared& ts) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int budget = min(p.budget, nb);
+  const int n_init = min(p.init, nb);
+  const int n_local = min(p.local, nb);
+  const int local_begin = nb - n_local;
+  const int n_forced = n_init + n_local - max(0, n_init - local_begin);
+  const int K = max(0, budget - n_forced);
+  auto forced = [&](int i) { return i < n_init || i >= local_begin; };
+  const int seg = (nb + kThreads - 1) / kThreads * 32;
+  const int lo = warp * seg, hi = min(nb, lo + seg);
+  const uint32_t lanes_below = (1u << lane) - 1u;
+
+  // keys, with every load of a batch in flight at once
+  constexpr int kLoadBatch = 16;
+  bool nan_seen = false;
+  for (int base = 0; base < nb; base += kThreads * kLoadBatch) {
+    float v[kLoadBatch];
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int i = base + u * kThreads + tid;
+      v[u] = i < nb ? __ldcg(scores + i) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int i = base + u * kThreads + tid;
+      if (i < nb) {
+        nan_seen |= isnan(v[u]);
+        keys[i] = float_order_key(v[u]);
+      }
+    }
+  }
+  if (nan_seen) raise_status(p.status, SA_DEV_NONFINITE);
+  for (int w = tid; w < (nb + 31) / 32; w += kThreads) ts.tie_bits[w] = 0;
+  for (int i = tid; i < 256; i += kThreads) ts.hist[0][i] = 0;
+  if (tid == 0) ts.ncand = 0;
+  __syncthreads();
+
+  // threshold bucket: `bucket` unforced blocks have (key & mask) == prefix,
+  // the first `remaining` of them (in the sort order) are chosen
+  uint32_t prefix = 0, mask = 0;
+  int remaining = K, bucket = nb - n_forced;
+  bool whole = true;  // every bucket member chosen; else tie_bits marks them
+  if (K > 0) {
+    for (int pass = 0;; ++pass) {
+      if (bucket == remaining) break;
+      if (bucket <= kTieMax) {
+        // gather the members (in any order) and rank each among them
+        for (int i = tid; i < nb; i += kThreads) {
+          const uint32_t k = keys[i];
+          if (!forced(i) && (k & mask) == prefix) {
+            const int s = atomicAdd(&ts.ncand, 1);
+            ts.cand_key[s] = k;
+            ts.cand_idx[s] = i;
+          }
+        }
+        __syncthreads();
+        if (tid < bucket) {
+          const uint32_t k = ts.cand_key[tid];
+          const int i = ts.cand_idx[tid];
+          int rank = 0;
+          for (int j = 0; j < bucket; ++j) {
+            const uint32_t kj = ts.cand_key[j];
+            rank += kj > k || (kj == k && ts.cand_idx[j] < i);
+          }
+          if (rank < remaining) atomicOr(&ts.tie_bits[i >> 5], 1u << (i & 31));
+        }
+        __syncthreads();
+        whole = false;
+        break;
+      }
+      if (pass == 4) {
+        // more than kTieMax equal keys: the first `remaining` by index
+        auto member = [&](int i) { return i < hi && !forced(i) && keys[i] == prefix; };
+        int n = 0;
+        for (int base = lo; base < hi; base += 32) n += __popc(__ballot_sync(kFull, member(base + lane)));
+        if (lane == 0) ts.warp_count[warp] = n;
+        __syncthreads();
+        int before = 0;
+        for (int w = 0; w < warp; ++w) before += ts.warp_count[w];
+        for (int base = lo; base < hi; base += 32) {
+          const bool m = member(base + lane);
+          const uint32_t b = __ballot_sync(kFull, m);
+          const uint32_t take =
+              __ballot_sync(kFull, m && before + __popc(b & lanes_below) < remaining);
+          if (lane == 0) ts.tie_bits[base >> 5] = take;
+          before += __popc(b);
+        }
+        __syncthreads();
+        whole = false;
+        break;
+      }
+      // histogram of the next 8 bits over the bucket; the other buffer is
+      // cleared for the pass after this one
+      const int shift = 24 - 8 * pass;
+      int* hist = ts.hist[pass & 1];
+      for (int i = tid; i < 256; i += kThreads) ts.hist[(pass + 1) & 1][i] = 0;
+#pragma unroll 4
+      for (int i = tid; i < nb; i += kThreads) {
+        const uint32_t k = keys[i];
+        if (!forced(i) && (k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1);
+      }
+      __syncthreads();
+      if (warp == 0) {
+        // digits in descending order: lane l holds digits 255 - 8l - j
+        int c[8];
+        int local = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          c[j] = hist[255 - 8 * lane - j];
+          local += c[j];
+        }
+        int incl = local;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int v = __shfl_up_sync(kFull, incl, o);
+          if (lane >= o) incl += v;
+        }
+        int acc = incl - local;
+        if (acc < remaining && remaining <= incl) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if (acc < remaining && acc + c[j] >= remaining) {
+              ts.digit = 255 - 8 * lane - j;
+              ts.above = acc;
+              ts.bucket = c[j];
+            }
+            acc += c[j];
+          }
+        }
+      }
+      __syncthreads();
+      prefix |= (uint32_t)ts.digit << shift;
+      mask |= 0xffu << shift;
+      remaining -= ts.above;
+      bucket = ts.bucket;
+    }
+  }
+
+  // chosen blocks in index order
+  auto chosen = [&](int i) {
+    if (i >= hi) return false;
+    if (forced(i)) return true;
+    if (K == 0) return false;
+    const uint32_t km = keys[i] & mask;
+    if (km != prefix) return km > prefix;
+    return whole || (ts.tie_bits[i >> 5] >> (i & 31) & 1u) != 0u;
+  };
+  int n = 0;
+#pragma unroll 4
+  for (int base = lo; base < hi; base += 32) {
+    const uint32_t b = __ballot_sync(kFull, chosen(base + lane));
+    if (lane == 0) ts.pick_bits[base >> 5] = b;
+    n += __popc(b);
+  }
+  if (lane == 0) ts.warp_count[warp] = n;
+  __syncthreads();
+  int pos = 0, total = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    const int c = ts.warp_count[w];
+    pos += w < warp ? c : 0;
+    total += c;
+  }
+  int32_t* ids = p.ids + (size_t)unit * p.budget;
+  for (int base = lo; base < hi; base += 32) {
+    const uint32_t b = ts.pick_bits[base >> 5];
+    if (b >> lane & 1u) {
+      const int at = pos + __popc(b & lanes_below);
+      if (at < p.budget) ids[at] = base + lane;
+    }
+    pos += __popc(b);
+  }
+  if (tid == 0 && p.counts) p.counts[unit] = min(total, p.budget);
+}
+
 __global__ void __launch_bounds__(kThreads)
     select_kernel(const SelectParams p, const int vec) {
   // dynamic shared memory: q [group][d], head dots [group][chunk], then (last
@@ -227,102 +427,7 @@ __global__ void __launch_bounds__(kThreads)
     if (!ts.last) return;
   }
 
-  uint32_t* keys = reinterpret_cast<uint32_t*>(smem);  // q and dots are no longer needed
-  const int budget = min(p.budget, nb);
-  const int n_init = min(p.init, nb);
-  const int n_local = min(p.local, nb);
-  const int local_begin = nb - n_local;
-  const int n_forced = n_init + n_local - max(0, n_init - local_begin);
-  const int K = max(0, budget - n_forced);
-  auto forced = [&](int i) { return i < n_init || i >= local_begin; };
-
-  bool nan_seen = false;
-  for (int i = threadIdx.x; i < nb; i += kThreads) {
-    const float sc = __ldcg(scores + i);
-    nan_seen |= isnan(sc);
-    keys[i] = float_order_key(sc);
-  }
-  if (nan_seen) raise_status(p.status, SA_DEV_NONFINITE);
-  __syncthreads();
-
-  uint32_t prefix = 0, mask = 0;
-  int remaining = K;
-  if (K > 0) {
-    for (int pass = 0; pass < 4; ++pass) {
-      const int shift = 24 - 8 * pass;
-      for (int i = threadIdx.x; i < 256; i += kThreads) ts.hist[i] = 0;
-      __syncthreads();
-      for (int i = threadIdx.x; i < nb; i += kThreads) {
-        if (forced(i)) continue;
-        const uint32_t k = keys[i];
-        if ((k & mask) == prefix) atomicAdd(&ts.hist[(k >> shift) & 255u], 1);
-      }
-      __syncthreads();
-      if (threadIdx.x < 32) {
-        const int lane = threadIdx.x;
-        int c[8];
-        int local = 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          c[j] = ts.hist[255 - 8 * lane - j];
-          local += c[j];
-        }
-        int incl = local;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int v = __shfl_up_sync(kFull, incl, o);
-          if (lane >= o) incl += v;
-        }
-        const int before = incl - local;
-        if (before < remaining && remaining <= incl) {
-          int acc = before;
-          bool found = false;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            if (!found && acc + c[j] >= remaining) {
-              ts.digit = 255 - 8 * lane - j;
-              ts.above = acc;
-              found = true;
-            }
-            acc += c[j];
-          }
-        }
-      }
-      __syncthreads();
-      prefix |= (uint32_t)ts.digit << shift;
-      mask |= 0xffu << shift;
-      remaining -= ts.above;
-      __syncthreads();
-    }
-  }
-  // Chosen: forced, or key above the threshold, or equal to it among the
-  // first `remaining` such blocks in index order.
-  const int per = (nb + kThreads - 1) / kThreads;
-  const int lo = min(nb, threadIdx.x * per);
-  const int hi = min(nb, lo + per);
-  int eq_local = 0;
-  if (K > 0)
-    for (int i = lo; i < hi; ++i) eq_local += (!forced(i) && keys[i] == prefix);
-  int eq_total = 0;
-  const int eq_before = block_exclusive_scan(eq_local, ts.scan, &eq_total);
-  auto chosen = [&](int i, int& eq_seen) {
-    if (forced(i)) return true;
-    if (K == 0) return false;
-    const uint32_t k = keys[i];
-    if (k > prefix) return true;
-    if (k == prefix) return eq_seen++ < remaining;
-    return false;
-  };
-  int cnt = 0;
-  int eq_seen = eq_before;
-  for (int i = lo; i < hi; ++i) cnt += chosen(i, eq_seen);
-  int total = 0;
-  int pos = block_exclusive_scan(cnt, ts.scan, &total);
-  int32_t* ids = p.ids + (size_t)unit * p.budget;
-  eq_seen = eq_before;
-  for (int i = lo; i < hi; ++i)
-    if (chosen(i, eq_seen) && pos < p.budget) ids[pos++] = i;
-  if (threadIdx.x == 0 && p.counts) p.counts[unit] = min(total, p.budget);
+  select_top_k(p, unit, nb, scores, reinterpret_cast<uint32_t*>(smem), ts);
 }
 
 }  // namespace
