@@ -15,7 +15,8 @@ max time. `--config cfg5` (one 128K-context sequence) shards the KV heads
 instead: rank r holds KH/N heads of every layer, and each step ends with an
 NCCL all-gather of the per-head outputs: strong scaling.
 
-`value` is device-timed with inputs resident in HBM; `e2e` runs the same
+`value` is device-timed with inputs resident in HBM, the timed steps replayed
+from one recorded CUDA graph (`--launch eager` issues one call per step); `e2e` runs the same
 steps through the public host-buffer call (sa_ctx_step_host: H2D of the
 step's query + new K/V, step, D2H of the output, synchronize).
 `--impl reference` times the reference's own CPU implementation (the C++
@@ -51,6 +52,9 @@ def parse_args():
     ap.add_argument("--config", default="cfg3", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--kernel-iters", type=int, default=50)
+    ap.add_argument("--launch", default="graph", choices=["graph", "eager"],
+                    help="timed steps replayed from one recorded CUDA graph (sa_ctx_graph_*) "
+                         "or launched one call at a time; KV-head sharding always runs eager")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
@@ -309,9 +313,11 @@ def main():
     else:
         kv_slice = None
         seq_offset = rank * w.seqs  # sequence sharding by global batch index
-    # table room for every append of the run: warmup + timed + e2e steps
-    ctx, info = workloads.make_context(w, total + e2e_steps + 64, dev, seed=1,
-                                       kv_heads_slice=kv_slice, seq_offset=seq_offset)
+    # table room for every append of the run: warmup + timed + e2e steps. The
+    # context's stream is its own (a graph cannot record the default stream).
+    with torch.cuda.stream(torch.cuda.Stream(dev)):
+        ctx, info = workloads.make_context(w, total + e2e_steps + 64, dev, seed=1,
+                                           kv_heads_slice=kv_slice, seq_offset=seq_offset)
     phase_bits = {}
     queries, kv_new = workloads.decode_inputs(w, info, total, dev, seed=1 + seq_offset,
                                               kv_heads_slice=kv_slice)
@@ -338,6 +344,12 @@ def main():
         for s in range(args.warmup):
             step(s)
     ctx.sync()
+    use_graph = args.launch == "graph" and not heads_mode
+    if use_graph:
+        # record the K timed steps (nothing runs); the timed region replays them
+        with torch.cuda.stream(stream), ctx.record():
+            for s in range(args.warmup, total):
+                step(s)
     barrier()
     torch.cuda.synchronize()
     launches0 = ctx.launches
@@ -347,8 +359,11 @@ def main():
     end = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         start.record(stream)
-        for s in range(args.warmup, total):
-            step(s)
+        if use_graph:
+            ctx.graph_launch()
+        else:
+            for s in range(args.warmup, total):
+                step(s)
         end.record(stream)
     end.synchronize()
     clock_info = clocks.stop()
@@ -498,7 +513,9 @@ def main():
                                 f"sequence-sharded x{world}" if world > 1 else "single"),
                 "l2": "inputs larger than L2: each step reads its selected KV and all "
                       "representatives (>1 GB at cfg3)",
-                "kv_dtype": "fp16", "accumulate": "fp32"},
+                "kv_dtype": "fp16", "accumulate": "fp32",
+                "launch": ("one CUDA graph of the timed steps (sa_ctx_graph_launch)" if use_graph
+                           else "one sa_ctx_step call per step")},
             "selected_kv_gbs": attn_gbs, "selected_kv_frac": attn_gbs / hbm,
             # selected KV (16-token average tail) per GPU-step x per-GPU steps/s
             "step_selected_kv_gbs": w.selected_kv_bytes(16) * steps_per_s / world / 1e9,

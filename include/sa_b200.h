@@ -326,6 +326,20 @@ SA_API sa_status sa_ctx_seal(sa_ctx* ctx);
 SA_API sa_status sa_ctx_sync(sa_ctx* ctx, uint32_t* bits_out);
 /* Kernel launches issued by the context since creation (for accounting). */
 SA_API uint64_t sa_ctx_launch_count(const sa_ctx* ctx);
+/* Decode-step graphs. No reference counterpart: the reference synchronises
+ * after every call (cpp/src/cuda_backend.cpp:397). Between
+ * sa_ctx_graph_begin and sa_ctx_graph_end the context's stream-ordered calls
+ * (sa_ctx_step, sa_ctx_step_raw, the stage calls, ...) are recorded into a
+ * CUDA graph instead of running; sa_ctx_graph_end instantiates and uploads
+ * the recording (replacing an earlier one) and sa_ctx_graph_launch replays it
+ * on the context's stream, reading and writing the device addresses the
+ * recorded calls named. Calls that synchronise or read host memory
+ * (sa_ctx_sync, sa_ctx_step_host, setup calls) are refused while a recording
+ * is open, and the context's stream must not be the legacy default stream.
+ * Replays run back to back without host launch gaps between the kernels. */
+SA_API sa_status sa_ctx_graph_begin(sa_ctx* ctx);
+SA_API sa_status sa_ctx_graph_end(sa_ctx* ctx);
+SA_API sa_status sa_ctx_graph_launch(sa_ctx* ctx);
 /* Quality audit of the selection (replaces audit_dense_selection,
  * cpp/src/pipeline_main.cpp:502-574, and the selected-vs-dense comparison of
  * cpp/src/selection_main.cpp:246-252): for every (seq, layer, KV head), the

@@ -17,6 +17,7 @@ Invalid dimensions raise :class:`SparseKVError` with status
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes as C
 import math
 
@@ -438,6 +439,34 @@ class DecodeContext:
     @property
     def launches(self) -> int:
         return int(self._lib.sa_ctx_launch_count(self._h))
+
+    # ---- decode-step graphs
+    def graph_begin(self) -> None:
+        """Start recording this context's stream-ordered calls into a CUDA
+        graph instead of running them (sa_ctx_graph_begin). The context must
+        have been created on a non-default stream."""
+        check(self._lib.sa_ctx_graph_begin(self._h), "sa_ctx_graph_begin")
+
+    def graph_end(self) -> None:
+        """Close the recording, instantiate and upload it (sa_ctx_graph_end)."""
+        check(self._lib.sa_ctx_graph_end(self._h), "sa_ctx_graph_end")
+
+    def graph_launch(self) -> None:
+        """Replay the recorded calls on the context's stream (sa_ctx_graph_launch)."""
+        check(self._lib.sa_ctx_graph_launch(self._h), "sa_ctx_graph_launch")
+
+    @contextlib.contextmanager
+    def record(self):
+        """`with ctx.record(): ctx.step(...)` records the calls of the block;
+        `ctx.graph_launch()` replays them."""
+        self.graph_begin()
+        try:
+            yield self
+        except BaseException:
+            # close the capture so the stream stays usable; the body's error wins
+            self._lib.sa_ctx_graph_end(self._h)
+            raise
+        self.graph_end()
 
     # ---- KV-head sharding: outputs gathered over peer memory
     def gather_buffer(self, world: int) -> tuple[int, int]:

@@ -105,6 +105,9 @@ PROTOTYPES = {
     "sa_ctx_seal": (C.c_int, [_vp]),
     "sa_ctx_sync": (C.c_int, [_vp, C.POINTER(C.c_uint32)]),
     "sa_ctx_launch_count": (C.c_uint64, [_vp]),
+    "sa_ctx_graph_begin": (C.c_int, [_vp]),
+    "sa_ctx_graph_end": (C.c_int, [_vp]),
+    "sa_ctx_graph_launch": (C.c_int, [_vp]),
     "sa_ctx_audit": (C.c_int, [_vp, _vp, _vp]),
     "sa_ctx_slot_correct": (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
     "sa_ctx_step_raw": (C.c_int, [_vp] * 7 + [C.c_float, C.c_float, _vp]),

@@ -154,7 +154,21 @@ struct sa_ctx {
   int gather_world = 0, gather_rank = -1;
   void** gather_peers = nullptr;  // device array [gather_world]
   uint64_t gather_attends = 0;
+  // decode-step graph: recorded between sa_ctx_graph_begin and _end
+  bool recording = false;
+  uint64_t launches_before_recording = 0;
+  uint64_t graph_launches = 0;  // kernel launches one replay issues
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t graph_exec = nullptr;
 };
+
+namespace {
+// Calls that synchronise or copy through host memory cannot be recorded into
+// a graph; they are refused while a recording is open.
+sa_status refuse_while_recording(const char* what) {
+  return fail(SA_ERR_INVALID_ARG, std::string(what) + ": not allowed while a graph is being recorded");
+}
+}  // namespace
 
 extern "C" {
 
@@ -807,7 +821,14 @@ SA_API sa_status sa_ctx_create(const sa_ctx_config* config, sa_ctx** out) {
 SA_API sa_status sa_ctx_destroy(sa_ctx* c) {
   if (!c) return SA_OK;
   DeviceGuard guard(c->cfg.device);
+  if (c->recording) {
+    cudaGraph_t partial = nullptr;
+    cudaStreamEndCapture(c->stream, &partial);
+    if (partial) cudaGraphDestroy(partial);
+  }
   if (c->stream) cudaStreamSynchronize(c->stream);
+  if (c->graph_exec) cudaGraphExecDestroy(c->graph_exec);
+  if (c->graph) cudaGraphDestroy(c->graph);
   CtxDev& d = c->dev;
   void* ptrs[] = {d.pool, d.reps, d.table, d.num_sealed, d.tail_block, d.tail_len, d.generation,
                   d.query_ring, d.free_list, d.free_top, d.seal_counters, d.status, c->selected,
@@ -842,6 +863,7 @@ SA_API sa_status sa_ctx_get_ptrs(sa_ctx* c, sa_ctx_ptrs* o) {
 
 SA_API sa_status sa_ctx_set_stream(sa_ctx* c, void* stream) {
   if (!c) return fail(SA_ERR_INVALID_ARG, "ctx: null");
+  if (c->recording) return refuse_while_recording("set_stream");
   DeviceGuard guard(c->cfg.device);
   if (c->stream) cudaStreamSynchronize(c->stream);
   if (c->own_stream && c->stream) cudaStreamDestroy(c->stream);
@@ -854,6 +876,7 @@ SA_API void* sa_ctx_stream(sa_ctx* c) { return c ? static_cast<void*>(c->stream)
 
 SA_API sa_status sa_ctx_reset(sa_ctx* c) {
   if (!c) return fail(SA_ERR_INVALID_ARG, "ctx: null");
+  if (c->recording) return refuse_while_recording("reset");
   DeviceGuard guard(c->cfg.device);
   const auto& g = c->cfg;
   const size_t nsl = c->num_sl;
@@ -876,6 +899,7 @@ SA_API sa_status sa_ctx_reset(sa_ctx* c) {
 SA_API sa_status sa_ctx_prefill(sa_ctx* c, int32_t seq, int32_t layer, int32_t blocks,
                                 int32_t* phys_out_host) {
   if (!c) return fail(SA_ERR_INVALID_ARG, "ctx: null");
+  if (c->recording) return refuse_while_recording("prefill");
   const auto& g = c->cfg;
   if (seq < 0 || seq >= g.seqs || layer < 0 || layer >= g.layers || blocks < 0)
     return fail(SA_ERR_INVALID_ARG, "prefill: seq/layer/blocks out of range");
@@ -1026,6 +1050,7 @@ SA_API sa_status sa_ctx_step_host(sa_ctx* c, const float* query_host, const void
                                   int32_t kv_fp32, void* out_host) {
   if (!c || !query_host || !kv_new_host || !out_host)
     return fail(SA_ERR_INVALID_ARG, "step_host: null argument");
+  if (c->recording) return refuse_while_recording("step_host");
   DeviceGuard guard(c->cfg.device);
   const auto& g = c->cfg;
   const size_t q_bytes = (size_t)c->num_sl * g.query_heads * kHeadDim * sizeof(float);
@@ -1060,6 +1085,7 @@ SA_API sa_status sa_ctx_step_host(sa_ctx* c, const float* query_host, const void
 
 SA_API sa_status sa_ctx_sync(sa_ctx* c, uint32_t* bits_out) {
   if (!c) return fail(SA_ERR_INVALID_ARG, "sync: null ctx");
+  if (c->recording) return refuse_while_recording("sync");
   DeviceGuard guard(c->cfg.device);
   SA_CUDA_TRY(cudaStreamSynchronize(c->stream));
   uint32_t bits = 0;
@@ -1071,6 +1097,54 @@ SA_API sa_status sa_ctx_sync(sa_ctx* c, uint32_t* bits_out) {
 }
 
 SA_API uint64_t sa_ctx_launch_count(const sa_ctx* c) { return c ? c->launches : 0; }
+
+SA_API sa_status sa_ctx_graph_begin(sa_ctx* c) {
+  if (!c) return fail(SA_ERR_INVALID_ARG, "graph_begin: null ctx");
+  if (c->recording) return fail(SA_ERR_INVALID_ARG, "graph_begin: a recording is already open");
+  if (c->stream == nullptr || c->stream == cudaStreamLegacy)
+    return fail(SA_ERR_UNSUPPORTED, "graph_begin: the legacy default stream cannot be recorded");
+  DeviceGuard guard(c->cfg.device);
+  SA_CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+  c->recording = true;
+  c->launches_before_recording = c->launches;
+  return SA_OK;
+}
+
+SA_API sa_status sa_ctx_graph_end(sa_ctx* c) {
+  if (!c) return fail(SA_ERR_INVALID_ARG, "graph_end: null ctx");
+  if (!c->recording) return fail(SA_ERR_INVALID_ARG, "graph_end: no recording is open");
+  DeviceGuard guard(c->cfg.device);
+  c->recording = false;
+  // recorded calls launched nothing yet
+  const uint64_t recorded = c->launches - c->launches_before_recording;
+  c->launches = c->launches_before_recording;
+  cudaGraph_t graph = nullptr;
+  SA_CUDA_TRY(cudaStreamEndCapture(c->stream, &graph));
+  cudaGraphExec_t exec = nullptr;
+  cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+  if (e == cudaSuccess) e = cudaGraphUpload(exec, c->stream);
+  if (e != cudaSuccess) {
+    if (exec) cudaGraphExecDestroy(exec);
+    cudaGraphDestroy(graph);
+    return cuda_status(e, "graph_end: instantiate");
+  }
+  if (c->graph_exec) cudaGraphExecDestroy(c->graph_exec);
+  if (c->graph) cudaGraphDestroy(c->graph);
+  c->graph = graph;
+  c->graph_exec = exec;
+  c->graph_launches = recorded;
+  return SA_OK;
+}
+
+SA_API sa_status sa_ctx_graph_launch(sa_ctx* c) {
+  if (!c) return fail(SA_ERR_INVALID_ARG, "graph_launch: null ctx");
+  if (c->recording) return refuse_while_recording("graph_launch");
+  if (!c->graph_exec) return fail(SA_ERR_INVALID_ARG, "graph_launch: nothing recorded");
+  DeviceGuard guard(c->cfg.device);
+  SA_CUDA_TRY(cudaGraphLaunch(c->graph_exec, c->stream));
+  c->launches += c->graph_launches;
+  return SA_OK;
+}
 
 SA_API sa_status sa_ctx_audit(sa_ctx* c, const float* query, float* mass_out) {
   if (!c || !query || !mass_out) return fail(SA_ERR_INVALID_ARG, "audit: null argument");
@@ -1167,6 +1241,7 @@ SA_API sa_status sa_ctx_gather_buffer(sa_ctx* c, int32_t world, void** buf_out,
                                       size_t* bytes_out) {
   if (!c || !buf_out || world < 1 || world > 64)
     return fail(SA_ERR_INVALID_ARG, "gather_buffer: bad argument");
+  if (c->recording) return refuse_while_recording("gather_buffer");
   if (c->gather_buf && c->gather_world != world)
     return fail(SA_ERR_INVALID_ARG, "gather_buffer: already allocated for another world size");
   DeviceGuard guard(c->cfg.device);
@@ -1188,6 +1263,7 @@ SA_API sa_status sa_ctx_gather_buffer(sa_ctx* c, int32_t world, void** buf_out,
 
 SA_API sa_status sa_ctx_gather_attach(sa_ctx* c, int32_t rank, void* const* peer_bufs) {
   if (!c || !peer_bufs) return fail(SA_ERR_INVALID_ARG, "gather_attach: null argument");
+  if (c->recording) return refuse_while_recording("gather_attach");
   if (!c->gather_buf) return fail(SA_ERR_INVALID_ARG, "gather_attach: call sa_ctx_gather_buffer first");
   if (rank < 0 || rank >= c->gather_world)
     return fail(SA_ERR_INVALID_ARG, "gather_attach: rank outside [0, world)");

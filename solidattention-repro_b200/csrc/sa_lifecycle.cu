@@ -38,6 +38,7 @@ struct RepSmem {
   uint16_t kT[kRepMaxDim][kRepKeyLd];           // keys, transposed [dim][key]
   float qbuf[kRepWarps][kRepMaxDim];            // one query row per warp
   float contrib[kRepMaxQueries][kBlockTokens];  // probability query -> block key
+  float qall[kBlockTokens][kRepMaxDim];         // every query row (one-warp calls)
   int order[kBlockTokens];
 };
 
@@ -90,19 +91,97 @@ __device__ void rep_block(const RepCall& c, RepSmem& s) {
   const int k_lo = max(0, p_lo - W + 1);
   const int nk = p_hi - k_lo;
 
+  // One-warp calls: every key of the call fits the 32 lanes of a warp (the
+  // seal of a block and per-block builds, window <= 32), and rows can be
+  // read 16 bytes at a time. A warp then scores four queries at once, lane =
+  // key, instead of one query per pass.
+  const bool one_warp = nk <= 32 && D == kRepMaxDim &&
+                        (reinterpret_cast<uintptr_t>(c.kv) & 15u) == 0 &&
+                        (c.head_major || c.row_stride % 8 == 0) &&
+                        (reinterpret_cast<uintptr_t>(c.q) & 15u) == 0;
   bool bad = false;
-  for (int idx = tid; idx < nk * D; idx += kRepThreads) {
-    const int r = idx / D, dim = idx - r * D;
-    const uint16_t* row = key_row(c, k_lo + r);
-    bad |= row == nullptr;
-    s.kT[dim][r] = row ? row[dim] : (uint16_t)0;
+  if (one_warp) {
+    constexpr int kChunks8 = kRepMaxDim / 8;
+#pragma unroll 2
+    for (int idx = tid; idx < nk * kChunks8; idx += kRepThreads) {
+      const int r = idx / kChunks8, c8 = idx - r * kChunks8;
+      const uint16_t* row = key_row(c, k_lo + r);
+      bad |= row == nullptr;
+      uint4 u = make_uint4(0u, 0u, 0u, 0u);
+      if (row) u = *reinterpret_cast<const uint4*>(row + c8 * 8);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        s.kT[c8 * 8 + 2 * j][r] = (uint16_t)(w[j] & 0xffffu);
+        s.kT[c8 * 8 + 2 * j + 1][r] = (uint16_t)(w[j] >> 16);
+      }
+    }
+    constexpr int kChunks4 = kRepMaxDim / 4;
+#pragma unroll 4
+    for (int idx = tid; idx < nq * kChunks4; idx += kRepThreads) {
+      const int qi = idx / kChunks4, c4 = idx - qi * kChunks4;
+      *reinterpret_cast<float4*>(&s.qall[qi][c4 * 4]) =
+          *reinterpret_cast<const float4*>(c.q + (int64_t)(p_lo + qi) * D + c4 * 4);
+    }
+  } else {
+    for (int idx = tid; idx < nk * D; idx += kRepThreads) {
+      const int r = idx / D, dim = idx - r * D;
+      const uint16_t* row = key_row(c, k_lo + r);
+      bad |= row == nullptr;
+      s.kT[dim][r] = row ? row[dim] : (uint16_t)0;
+    }
   }
   if (bad) raise_status(c.status, SA_DEV_BAD_BLOCK);
   for (int idx = tid; idx < nq * kBlockTokens; idx += kRepThreads)
     s.contrib[idx / kBlockTokens][idx % kBlockTokens] = 0.f;
   __syncthreads();
 
-  for (int qi = warp; qi < nq; qi += kRepWarps) {
+  if (one_warp) {
+    // lane = key k_lo + lane; a warp takes queries q0 + j * kRepWarps, j < 4.
+    // Each dot keeps the reference's order (sequential over dims, multiply
+    // and add rounded separately); lanes outside a query's window compute a
+    // dot that is discarded, and their zero terms leave the ordered
+    // denominator unchanged.
+    const int key = k_lo + lane;
+    for (int q0 = warp; q0 < nq; q0 += 4 * kRepWarps) {
+      const float* qr[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) qr[j] = s.qall[min(q0 + j * kRepWarps, nq - 1)];
+      float dot[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+      for (int dim = 0; dim < kRepMaxDim; dim += 4) {
+        float kf[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) kf[u] = h2f(s.kT[dim + u][lane]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float4 qv = *reinterpret_cast<const float4*>(qr[j] + dim);
+          dot[j] = __fadd_rn(dot[j], __fmul_rn(qv.x, kf[0]));
+          dot[j] = __fadd_rn(dot[j], __fmul_rn(qv.y, kf[1]));
+          dot[j] = __fadd_rn(dot[j], __fmul_rn(qv.z, kf[2]));
+          dot[j] = __fadd_rn(dot[j], __fmul_rn(qv.w, kf[3]));
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int qi = q0 + j * kRepWarps;
+        if (qi >= nq) break;
+        const int pos = p_lo + qi;
+        const bool valid = lane < nk && key >= max(0, pos - W + 1) && key <= pos;
+        const float lg = valid ? __fmul_rn(dot[j], c.scale) : -INFINITY;
+        float maxv = lg;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) maxv = fmaxf(maxv, __shfl_xor_sync(kFull, maxv, o));
+        const float e = valid ? expf(__fsub_rn(lg, maxv)) : 0.f;
+        float den = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) den = __fadd_rn(den, __shfl_sync(kFull, e, i));
+        if (valid && key >= blk0 && key < blk0 + kBlockTokens)
+          s.contrib[qi][key - blk0] = __fdiv_rn(e, den);
+      }
+    }
+  }
+  for (int qi = one_warp ? nq : warp; qi < nq; qi += kRepWarps) {
     const int pos = p_lo + qi;
     const float* qrow = c.q + (int64_t)pos * D;
     for (int dim = lane; dim < D; dim += 32) s.qbuf[warp][dim] = qrow[dim];
@@ -306,11 +385,18 @@ __global__ void __launch_bounds__(kRepThreads) seal_kernel(const CtxDev c, int p
   pdl_launch_dependents();
   pdl_wait();  // the attention of this step still reads the tails
   const int items = c.qh * c.num_sl;
-  for (int i = blockIdx.x; i < items; i += gridDim.x) {
-    seal_rebuild(c, i % c.qh, i / c.qh, pending);
-    __syncthreads();  // the next item reuses the shared buffers
+  // Most steps fill no tail: test all of this CTA's items in one round of
+  // loads (one item per thread) before walking them one at a time.
+  int full = 0;
+  for (int i = blockIdx.x + (int)threadIdx.x * (int)gridDim.x; i < items;
+       i += (int)(blockDim.x * gridDim.x))
+    full |= effective_tail(c, i / c.qh, pending) >= kBlockTokens;
+  if (__syncthreads_or(full)) {
+    for (int i = blockIdx.x; i < items; i += gridDim.x) {
+      seal_rebuild(c, i % c.qh, i / c.qh, pending);
+      __syncthreads();  // the next item reuses the shared buffers
+    }
   }
-  __syncthreads();
   if (threadIdx.x == 0) {
     // the barrier orders the CTA's representative stores before this fence
     __threadfence();

@@ -425,6 +425,47 @@ def test_step_host_matches_device_step_pinned_and_pageable(pkg, cuda):
         c.close()
 
 
+def test_recorded_steps_replay_like_eager_steps(pkg, cuda):
+    """sa_ctx_graph_begin / _end / _launch: decode steps recorded into a CUDA
+    graph and replayed give the eager steps' outputs and state bit for bit,
+    across a seal; synchronising calls are refused while recording."""
+    import dataclasses
+
+    from solidattention_repro_b200 import SparseKVError, workloads
+
+    w = dataclasses.replace(workloads.CONFIGS["cfg2"], name="graph-step-test", layers=2,
+                            context_blocks=40, budget_blocks=12, hot_blocks=2)
+    steps = 34
+    eager, info = workloads.make_context(w, steps, cuda, seed=9)
+    side = torch.cuda.Stream(cuda)
+    with torch.cuda.stream(side):
+        rec, _ = workloads.make_context(w, steps, cuda, seed=9)
+    q, kv = workloads.decode_inputs(w, info, steps, cuda, seed=9)
+    outs = [rec.new_output() for _ in range(steps)]
+    torch.cuda.synchronize(cuda)
+    launches = rec.launches
+    with rec.record():
+        for s in range(steps):
+            rec.step(q[s], kv[s], outs[s])
+        with pytest.raises(SparseKVError):
+            rec.sync()
+    assert rec.launches == launches  # recording launches nothing
+    assert int(rec.tail_len.cpu()[0]) == int(eager.tail_len.cpu()[0])
+    rec.graph_launch()
+    rec.sync()
+    want = [eager.step(q[s], kv[s]) for s in range(steps)]
+    eager.sync()
+    for s in range(steps):
+        assert torch.equal(outs[s], want[s]), s
+    assert rec.launches - launches == eager.launches - launches
+    for name in ("num_sealed", "tail_len", "tail_block", "generation", "selected", "reps"):
+        assert torch.equal(getattr(rec, name), getattr(eager, name)), name
+    assert (eager.generation.cpu().numpy() == 1).all()  # the 32nd append sealed
+    for c in (rec, eager):
+        assert c.status_bits() == 0
+        c.close()
+
+
 def test_slot_table_follows_the_selection_bit_exact(pkg, port, cuda):
     """sa_ctx_slot_correct over a decode loop: a resident window that starts
     empty and follows each step's selection equals the oracle's
