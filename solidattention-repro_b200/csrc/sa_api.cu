@@ -1,11 +1,10 @@
 // sa_api.cu -- implementation of the C ABI declared in include/sa_b200.h.
 //
 // Host-side runtime of the sparse-KV path: argument validation with the
-// reference's error conditions, TMA descriptor creation, workspace plans,
+// reference's error conditions, workspace plans,
 // the AcceleratorBackend-style handle (host buffers, event timings) and the
 // paged decode context (pool, free list, block tables, tails, seal).
 #include <cuda.h>
-#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -36,20 +35,6 @@ sa_status cuda_status(cudaError_t err, const char* what) {
 
 namespace {
 
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
 // Runs the caller's device choice on entry and restores it on exit.
 class DeviceGuard {
  public:
@@ -76,26 +61,6 @@ sa_status ensure_smem_limit(const void* kernel, int bytes, int* configured_per_d
   if (configured_per_device[dev] >= bytes) return SA_OK;
   SA_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
   configured_per_device[dev] = bytes;
-  return SA_OK;
-}
-
-sa_status make_row_tensor_map(CUtensorMap* map, const void* base, uint64_t row_elems,
-                              uint64_t rows) {
-  auto encode = tensor_map_encoder();
-  if (!encode) return fail(SA_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
-  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
-    return fail(SA_ERR_INVALID_ARG, "KV buffer must be 16-byte aligned");
-  if (rows == 0 || rows > 0xffffffffull) return fail(SA_ERR_UNSUPPORTED, "KV rows out of TMA range");
-  const cuuint64_t dims[2] = {row_elems, rows};
-  const cuuint64_t strides[1] = {row_elems * sizeof(uint16_t)};
-  const cuuint32_t box[2] = {(cuuint32_t)kHeadDim, (cuuint32_t)kBlockTokens};
-  const cuuint32_t elem_strides[2] = {1, 1};
-  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims,
-                            strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS)
-    return fail(SA_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
   return SA_OK;
 }
 
@@ -130,7 +95,6 @@ struct sa_ctx {
   cudaStream_t stream = nullptr;
   bool own_stream = false;
   CtxDev dev{};
-  CUtensorMap pool_map{};
   int32_t* selected = nullptr;
   int32_t* selected_count = nullptr;
   float* scores = nullptr;
@@ -213,15 +177,16 @@ SA_API sa_status sa_attention_packed(const uint16_t* kv, const float* query, siz
   if (!workspace || workspace_bytes < need)
     return fail(SA_ERR_CAPACITY, "attention: workspace smaller than sa_attention_workspace_size()");
   if (tokens > 0xffffffffull) return fail(SA_ERR_UNSUPPORTED, "attention: too many tokens");
+  if ((reinterpret_cast<uintptr_t>(kv) & 15u) != 0)
+    return fail(SA_ERR_INVALID_ARG, "KV buffer must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  CUtensorMap map;
-  sa_status st = make_row_tensor_map(&map, kv, 2 * kv_heads * kHeadDim, tokens);
-  if (st != SA_OK) return st;
   const int entries = (int)((tokens + kBlockTokens - 1) / kBlockTokens);
   const int units = (int)kv_heads;
   AttnParams p{};
   p.pool = nullptr;
   p.head_major = 0;
+  p.rows = kv;
+  p.row_bytes = (int64_t)(2 * kv_heads * kHeadDim * sizeof(uint16_t));
   p.kv_heads = (int)kv_heads;
   p.group = (int)(query_heads / kv_heads);
   p.num_sl = 1;
@@ -252,7 +217,7 @@ SA_API sa_status sa_attention_packed(const uint16_t* kv, const float* query, siz
   p.counters = reinterpret_cast<int*>(ws + ((partial_bytes + 255) & ~size_t(255)));
   p.status = nullptr;
   SA_CUDA_TRY(cudaMemsetAsync(p.counters, 0, (size_t)units * sizeof(int), s));
-  return launch_attention(p, map, s);
+  return launch_attention(p, s);
 }
 
 SA_API size_t sa_select_workspace_size(size_t query_heads, size_t group, size_t blocks) {
@@ -721,7 +686,7 @@ sa_status ctx_attend(sa_ctx* c, const float* query, void* out, int pending = 0,
     p.gather_counter_bytes = c->gather_counter_bytes;
   }
   ++c->launches;
-  const sa_status st = launch_attention(p, c->pool_map, c->stream);
+  const sa_status st = launch_attention(p, c->stream);
   if (st == SA_OK && c->gather_peers) ++c->gather_attends;
   return st;
 }
@@ -797,8 +762,6 @@ SA_API sa_status sa_ctx_create(const sa_ctx_config* config, sa_ctx** out) {
     st = cuda_status(cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->h_status_dev),
                                               c->h_status, 0),
                      "cudaHostGetDevicePointer status");
-  // The pool is head-major and read with bulk copies: no tensor map.
-  std::memset(&c->pool_map, 0, sizeof(c->pool_map));
   if (st == SA_OK) {
     SA_CUDA_TRY(cudaMemset(d.pool, 0, (size_t)g.pool_blocks * kBlockTokens * row_elems * 2));
     SA_CUDA_TRY(cudaMemset(d.reps, 0, nsl * g.query_heads * kHeadDim * (size_t)c->table_pad * 4));

@@ -19,12 +19,17 @@
 //
 // Pipeline: a stage holds two entries of one segment (2 x 16 KB: the K rows
 // then the V rows of the unit's KV head, 32 x 256 B each) in a ring of three
-// stages. Entries of the decode context's head-major pool arrive as one
-// contiguous 16 KB bulk copy; entries of a caller's token-major buffer as two
-// 8 KB TMA tiles (32 rows x 256 B) -- the shared-memory layout is the same.
-// A stage's loads complete a "full" mbarrier (bounded waits); the last of the
-// eight warps to release a stage (a shared-memory arrival counter) issues the
-// loads that refill it, so no warp ever blocks on a producer.
+// stages. Every lane reads only its own sixteen-byte column of its own rows
+// (below), so every lane also loads exactly those bytes itself, with 16-byte
+// cp.async copies through the load/store unit, one commit group per stage: a
+// lane waits only for its own copies and refills its part of a stage as soon
+// as it has computed on it, with no producer thread and no cross-warp release.
+// (On a B200, streaming random 16 KB blocks: one thread per SM issuing 16 KB
+// bulk copies read at most 4.3 TB/s and two such threads per SM 6.6 TB/s,
+// whatever the number of copies in flight, while 16-byte cp.async copies
+// reached 7.2 TB/s with 128 KB in flight per SM.) Rows come from the decode
+// context's head-major pool or from a caller's token-major rows; the
+// shared-memory layout is the same.
 //
 // Warp w, per stage: half-warp h takes entry h of the stage and its tokens
 // [4w, 4w+4); lane l covers head dims [8(l%16), 8(l%16)+8). A quarter-warp
@@ -118,12 +123,8 @@ struct alignas(128) AttnSmem {
   int seg_index[kMaxSegments];       // the CTA's place among its unit's CTAs
   int seg_count[kMaxSegments];       // CTAs covering the unit
   alignas(16) uint8_t ostage[G * kHeadDim * 4];  // a unit's output, for peer stores
-  uint64_t full[kStages];
-  int released[kStages];      // warps done with the stage's current contents
-  int stage_issues[kStages];  // loads issued into the stage so far
   int nseg;
   int nstages;
-  int abort_flag;
   int last_flag;
 };
 
@@ -210,36 +211,40 @@ __device__ __forceinline__ void load_pairs(const float2* src, float2 (&v)[G]) {
   }
 }
 
-// Issues the loads of stage j: one 16 KB bulk copy per entry from a
-// head-major pool, or two 8 KB TMA tiles per entry from a token-major buffer.
+// This lane's copies for stage j into shared-memory stage `slot`: rows
+// [t0, t0 + 4) of entry `half`, K then V plane, 16 bytes at column l16 --
+// exactly the bytes the lane reads; rows at or past the entry's token count
+// are not copied (the compute masks them).
 template <int G, bool kHeadMajor>
-__device__ __forceinline__ void issue_stage(AttnSmem<G>& s, const CUtensorMap* map,
-                                            const uint8_t* pool, int kv_heads, int j) {
-  const int stage = j % kStages;
+__device__ __forceinline__ void load_stage(AttnSmem<G>& s, const AttnParams& p, int j, int slot,
+                                           int half, int t0, int l16) {
   const uint32_t w = s.stage_info[j];
-  const int e0 = info_e0(w);
-  const int kvh = s.seg_unit[info_seg(w)] % kv_heads;
-  const uint32_t tx = (info_ntok(w, 0) > 0 ? kEntryBytes : 0) + (info_ntok(w, 1) > 0 ? kEntryBytes : 0);
-  if (tx) {
-    mbar_arrive_expect_tx(&s.full[stage], tx);
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      if (info_ntok(w, i) <= 0) continue;
-      uint8_t* dst = s.tiles[stage] + i * kEntryBytes;
-      const int phys = s.ent_phys[e0 + i];
-      if constexpr (kHeadMajor) {
-        bulk_load(dst, pool + ((size_t)phys * kv_heads + kvh) * kEntryBytes, kEntryBytes,
-                  &s.full[stage]);
-      } else {
-        const int y = phys * kBlockTokens;
-        tma_load_2d(dst, map, &s.full[stage], kvh * kHeadDim, y);
-        tma_load_2d(dst + kPlaneBytes, map, &s.full[stage], (kv_heads + kvh) * kHeadDim, y);
-      }
-    }
+  const int ntok = info_ntok(w, half);
+  if (ntok <= t0) return;
+  const int phys = s.ent_phys[info_e0(w) + half];
+  const int kvh = s.seg_unit[info_seg(w)] % p.kv_heads;
+  const uint8_t* src;
+  size_t row_stride, plane;
+  if constexpr (kHeadMajor) {
+    src = reinterpret_cast<const uint8_t*>(p.pool) +
+          ((size_t)phys * p.kv_heads + kvh) * kEntryBytes + (size_t)t0 * kRowBytes;
+    row_stride = kRowBytes;
+    plane = kPlaneBytes;
   } else {
-    mbar_arrive(&s.full[stage]);
+    src = reinterpret_cast<const uint8_t*>(p.rows) +
+          ((size_t)phys * kBlockTokens + t0) * (size_t)p.row_bytes + (size_t)kvh * kRowBytes;
+    row_stride = (size_t)p.row_bytes;
+    plane = (size_t)p.kv_heads * kRowBytes;
   }
-  s.stage_issues[stage] += 1;
+  src += l16 * 16;
+  uint8_t* dst = s.tiles[slot] + half * kEntryBytes + t0 * kRowBytes + l16 * 16;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    if (t0 + r < ntok) {
+      cp_async16(dst + r * kRowBytes, src + r * row_stride);
+      cp_async16(dst + kPlaneBytes + r * kRowBytes, src + plane + r * row_stride);
+    }
+  }
 }
 
 // Stores output element idx of unit u (local layout) and, when gathering,
@@ -309,7 +314,7 @@ __device__ __forceinline__ void pv_tokens(const uint8_t* vrow, const float2 (*pb
 
 template <int G, bool kHeadMajor>
 __global__ void __launch_bounds__(kThreads * virt_ctas<G>(), 1)
-    attention_kernel(const __grid_constant__ CUtensorMap map, const AttnParams p) {
+    attention_kernel(const AttnParams p) {
   // Pairs (token, head) per half-warp: 4G over 16 lanes -> VPL per lane.
   constexpr int NPH = 4 * G;
   constexpr int VPL = NPH > 16 ? NPH / 16 : 1;
@@ -318,7 +323,6 @@ __global__ void __launch_bounds__(kThreads * virt_ctas<G>(), 1)
   if (vbid<virt_ctas<G>()>() >= p.ctas) return;  // the idle half of an odd plan
   AttnSmem<G>& s = *reinterpret_cast<AttnSmem<G>*>(
       smem_raw + (size_t)vhalf<virt_ctas<G>()>() * sizeof(AttnSmem<G>));
-  const uint8_t* pool = reinterpret_cast<const uint8_t*>(p.pool);
   const int warp = vtid<virt_ctas<G>()>() >> 5;
   const int lane = vtid<virt_ctas<G>()>() & 31;
   pdl_launch_dependents();
@@ -331,12 +335,6 @@ __global__ void __launch_bounds__(kThreads * virt_ctas<G>(), 1)
   const int n = (int)min(hi - lo, (long long)kMaxCtaSlots);
   if (vtid<virt_ctas<G>()>() == 0) {
     if (hi - lo > kMaxCtaSlots) raise_status(p.status, SA_DEV_BAD_BLOCK);
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&s.full[i], 1);
-      s.released[i] = 0;
-      s.stage_issues[i] = 0;
-    }
-    s.abort_flag = 0;
     int nseg = 0, stages = 0;
     if (n > 0) {
       const long long u0 = lo / E;
@@ -362,8 +360,6 @@ __global__ void __launch_bounds__(kThreads * virt_ctas<G>(), 1)
     s.seg_stage0[nseg] = stages;
     s.nseg = nseg;
     s.nstages = stages;
-    mbar_fence_init();
-    if constexpr (!kHeadMajor) tma_prefetch_desc(&map);
   }
   pdl_wait();  // the selection (and the append) of this step
   for (int i = vtid<virt_ctas<G>()>(); i < n; i += kThreads) {
@@ -396,9 +392,6 @@ __global__ void __launch_bounds__(kThreads * virt_ctas<G>(), 1)
   }
   vsync<virt_ctas<G>()>();
   const int nstages = s.nstages;
-  if (vtid<virt_ctas<G>()>() == 0)
-    for (int j = 0; j < min(kStages, nstages); ++j)
-      issue_stage<G, kHeadMajor>(s, &map, pool, p.kv_heads, j);
 
   const int half = lane >> 4;      // which entry of the stage
   const int l16 = lane & 15;       // 16 B (8 dims) column of a 256 B row
@@ -412,12 +405,17 @@ __global__ void __launch_bounds__(kThreads * virt_ctas<G>(), 1)
   const bool pair_writer = (l16 & ((1 << kPairShift) - 1)) == 0;
   // Byte offsets of this lane's 16 B column in its entry's K plane, per token.
   const int col_off = half * kEntryBytes + t0 * kRowBytes + l16 * 16;
+  // one commit group per stage, the first kStages in flight before the loop
+#pragma unroll
+  for (int j = 0; j < kStages; ++j) {
+    if (j < nstages) load_stage<G, kHeadMajor>(s, p, j, j, half, t0, l16);
+    cp_async_commit();
+  }
 
   float m_run[VPL], m_thr[VPL], l_run[VPL];
   float2 acc[G][4];
   float2 q[G][4];  // q[g] holds head g ^ gsw
   int stage = 0;
-  uint32_t phase = 0;
 
   for (int j = 0; j < nstages; ++j) {
     const uint32_t info = s.stage_info[j];
@@ -443,16 +441,11 @@ __global__ void __launch_bounds__(kThreads * virt_ctas<G>(), 1)
         l_run[i] = 0.f;
       }
     }
-    // After a timed-out wait the CTA stops waiting and computing but keeps
-    // every barrier and counter step, so all warps stay in step.
-    bool ok = !*reinterpret_cast<volatile int*>(&s.abort_flag);
-    if (ok) ok = mbar_wait_bounded(&s.full[stage], phase, p.status);
-    ok = __all_sync(kFull, ok);
-    if (!ok && lane == 0) atomicExch(&s.abort_flag, 1);
+    cp_async_wait<kStages - 1>();  // this lane's copies of stage j have landed
     const int ntok = info_ntok(info, half);
     const int ntok_other = info_ntok(info, half ^ 1);
     const uint8_t* tile = s.tiles[stage];
-    if (ok && (t0 < ntok || t0 < ntok_other)) {
+    if (t0 < ntok || t0 < ntok_other) {
       const uint8_t* kcol = tile + col_off;
       // ---- QK over this lane's 8 dims, 4 tokens x G heads (permuted order) ----
       float part[NPH];
@@ -638,34 +631,17 @@ __global__ void __launch_bounds__(kThreads * virt_ctas<G>(), 1)
       vsync<virt_ctas<G>()>();  // the stage buffer is free again
     }
 
-    // Release the stage; its last user refills it with stage j + kStages.
-    if (lane == 0) {
-      __threadfence_block();
-      if (atomicAdd(&s.released[stage], 1) == kConsumerWarps - 1) {
-        s.released[stage] = 0;
-        __threadfence_block();
-        fence_proxy_async_shared();
-        if (j + kStages < nstages && !*reinterpret_cast<volatile int*>(&s.abort_flag))
-          issue_stage<G, kHeadMajor>(s, &map, pool, p.kv_heads, j + kStages);
-      }
-    }
-    if (++stage == kStages) {
-      stage = 0;
-      phase ^= 1u;
-    }
+    // Refill this lane's part of the stage with stage j + kStages (after a
+    // segment end only now: the merge used the stage as scratch).
+    if (j + kStages < nstages) load_stage<G, kHeadMajor>(s, p, j + kStages, stage, half, t0, l16);
+    cp_async_commit();
+    if (++stage == kStages) stage = 0;
   }
-
-  vsync<virt_ctas<G>()>();
-  if (s.abort_flag && vtid<virt_ctas<G>()>() == 0) {
-    // Let the loads still in flight land (bounded) before the CTA exits.
-    for (int st = 0; st < kStages; ++st)
-      if (s.stage_issues[st] > 0)
-        mbar_wait_bounded(&s.full[st], (s.stage_issues[st] - 1) & 1, p.status);
-  }
+  cp_async_wait<0>();  // only empty groups remain; nothing lands after exit
 }
 
 template <int G, bool kHeadMajor>
-sa_status launch_layout(const AttnParams& p, const CUtensorMap& map, cudaStream_t stream) {
+sa_status launch_layout(const AttnParams& p, cudaStream_t stream) {
   constexpr int kV = virt_ctas<G>();
   const size_t smem = kV * sizeof(AttnSmem<G>);
   static int configured[kMaxDevices];
@@ -674,15 +650,14 @@ sa_status launch_layout(const AttnParams& p, const CUtensorMap& map, cudaStream_
   if (st != SA_OK) return st;
   const cudaError_t e = launch_kernel(attention_kernel<G, kHeadMajor>, dim3((p.ctas + kV - 1) / kV),
                                       dim3(kThreads * kV),
-                                      smem, stream, p.pdl != 0, map, p);
+                                      smem, stream, p.pdl != 0, p);
   if (e != cudaSuccess) return cuda_status(e, "attention_kernel launch");
   return cuda_status(cudaGetLastError(), "attention_kernel launch");
 }
 
 template <int G>
-sa_status launch_g(const AttnParams& p, const CUtensorMap& map, cudaStream_t stream) {
-  return p.head_major ? launch_layout<G, true>(p, map, stream)
-                      : launch_layout<G, false>(p, map, stream);
+sa_status launch_g(const AttnParams& p, cudaStream_t stream) {
+  return p.head_major ? launch_layout<G, true>(p, stream) : launch_layout<G, false>(p, stream);
 }
 
 __global__ void gather_wait_kernel(const unsigned long long* counter, unsigned long long expected,
@@ -772,13 +747,13 @@ size_t attention_scratch_bytes(const AttnPlan& plan, int units, int group) {
   return (size_t)units * plan.max_segments * group * kPartialStride * sizeof(float);
 }
 
-sa_status launch_attention(const AttnParams& p, const CUtensorMap& map, cudaStream_t stream) {
+sa_status launch_attention(const AttnParams& p, cudaStream_t stream) {
   if (p.num_sl <= 0 || p.kv_heads <= 0 || p.ctas <= 0) return SA_OK;
   switch (p.group) {
-    case 1: return launch_g<1>(p, map, stream);
-    case 2: return launch_g<2>(p, map, stream);
-    case 4: return launch_g<4>(p, map, stream);
-    case 8: return launch_g<8>(p, map, stream);
+    case 1: return launch_g<1>(p, stream);
+    case 2: return launch_g<2>(p, stream);
+    case 4: return launch_g<4>(p, stream);
+    case 8: return launch_g<8>(p, stream);
     default: return fail(SA_ERR_UNSUPPORTED, "attention: query heads per KV head must be 1, 2, 4 or 8");
   }
 }

@@ -1,6 +1,6 @@
 // sa_device.cuh -- device-side helpers shared by the sm_100a kernels:
-// status bits, FP16 conversion, mbarrier + TMA (cp.async.bulk.tensor) wrappers
-// with bounded waits, and small block-wide scans.
+// status bits, 16-byte cp.async copies, FP16 conversion, small block-wide
+// scans, programmatic-launch hooks and the decode-tail append.
 #pragma once
 
 #include <cuda.h>
@@ -25,86 +25,24 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-// ---- mbarrier ------------------------------------------------------------
+// ---- cp.async (16-byte copies through the load/store unit) ------------------
 
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_fence_init() {
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
-               "r"(bytes)
+// Asynchronous 16-byte copy global -> shared (both 16-byte aligned); it lands
+// when a later cp_async_wait covers its commit group.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)),
+               "l"(reinterpret_cast<uint64_t>(src))
                : "memory");
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(done)
-      : "r"(smem_addr(bar)), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-
-// Waits for the phase with the given parity; false (and SA_DEV_TIMEOUT) if
-// it did not complete within kWaitLimitCycles. try_wait itself suspends the
-// thread for a while, so the clock is read only every 16 attempts.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
-                                                  uint32_t* status) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const long long start = clock64();
-  for (unsigned i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 15u) == 0 && clock64() - start > kWaitLimitCycles) {
-      raise_status(status, SA_DEV_TIMEOUT);
-      return false;
-    }
-  }
-}
-
-// ---- TMA -------------------------------------------------------------------
-
-// 2-D tiled load of the map's box at coordinates (x, y) into
-// shared memory, completing `bar`'s transaction count. No cluster multicast.
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
-                                            int32_t x, int32_t y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
-      : "memory");
-}
-
-// Orders this thread's earlier generic-proxy shared-memory accesses before
-// later async-proxy (TMA) accesses to the same memory.
-__device__ __forceinline__ void fence_proxy_async_shared() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-// Contiguous bulk copy global -> shared completing `bar`'s transaction count
-// (both addresses 16-byte aligned, bytes a multiple of 16). No multicast.
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
-                                          uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-          "r"(smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
-  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+// Waits until at most N of this thread's commit groups are still in flight.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // ---- conversions -----------------------------------------------------------

@@ -51,13 +51,6 @@ cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
 sa_status ensure_smem_limit(const void* kernel, int bytes, int* configured_per_device);
 constexpr int kMaxDevices = 64;
 
-// ---- TMA descriptors ---------------------------------------------------------
-
-// 2-D tensor map over token rows: x = FP16 element within a row of
-// `row_elems`, y = row. Box {128 elements (256 B), 32 rows}, no swizzle.
-sa_status make_row_tensor_map(CUtensorMap* map, const void* base, uint64_t row_elems,
-                              uint64_t rows);
-
 // ---- decode-context device state (owned by sa_api.cu) -------------------------
 
 struct CtxDev {
@@ -87,7 +80,9 @@ struct CtxDev {
 
 struct AttnParams {
   const void* pool;      // head-major pool base (used when head_major)
-  int head_major;        // 1: [block][KV head][K,V][32][128]; 0: token rows via the map
+  int head_major;        // 1: [block][KV head][K,V][32][128]; 0: token rows at `rows`
+  const void* rows;      // token-major rows [token][K,V][KV head][128] FP16 (head_major 0)
+  int64_t row_bytes;     // bytes per token row (16-byte multiple)
   int kv_heads;          // KV heads in a pool row
   int group;             // query heads per KV head (1, 2, 4, 8)
   int num_sl;            // (sequence, layer) pairs
@@ -141,7 +136,7 @@ struct AttnPlan {
 };
 AttnPlan attention_plan(int units, int slots_per_unit, int group);
 size_t attention_scratch_bytes(const AttnPlan& plan, int units, int group);
-sa_status launch_attention(const AttnParams& p, const CUtensorMap& map, cudaStream_t stream);
+sa_status launch_attention(const AttnParams& p, cudaStream_t stream);
 // Waits (bounded, one thread) until *counter >= expected with system-scope
 // acquire; SA_DEV_TIMEOUT in *status when it gives up.
 sa_status launch_gather_wait(const unsigned long long* counter, unsigned long long expected,
