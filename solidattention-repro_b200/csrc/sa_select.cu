@@ -43,10 +43,14 @@ constexpr unsigned kFull = 0xffffffffu;
 
 constexpr int kTieMax = kThreads;  // threshold buckets this small are ranked directly
 
+// Units of at most this many blocks keep their order keys in shared memory;
+// larger ones recompute them from the scores (L2) on every pass, so that the
+// dynamic shared memory every CTA reserves stays small (at 4096 blocks a
+// 16 KB key array cut the resident CTAs of the scoring from 10 to 9 per SM).
+constexpr int kSmemKeyBlocks = 2048;
+
 struct TopkShared {
   int hist[2][256];                 // radix histograms, double-buffered by pass
-  uint32_t tie_bits[kMaxBlocks / 32];   // chosen members of the threshold bucket
-  uint32_t pick_bits[kMaxBlocks / 32];  // chosen blocks, for the ordered compaction
   uint32_t cand_key[kTieMax];       // threshold-bucket members gathered for ranking
   int cand_idx[kTieMax];
   int digit;
@@ -181,8 +185,25 @@ __device__ void raw_projections(const SelectParams& p, int sl, int g, float* qs,
 // blocks [w * seg, (w + 1) * seg), seg a multiple of 32, one block per lane
 // per step, so a ballot keeps index order inside a warp and one exchange of
 // warp totals keeps it across warps.
+// Dynamic shared memory of the top-k: [keys (nb_cap, kSmemKeys only)]
+// [tie_bits][pick_bits] (nb_cap / 32 words each): the chosen members of the
+// threshold bucket, and the chosen blocks for the ordered compaction.
+__host__ __device__ __forceinline__ int bitmap_words(int nb_cap) { return (nb_cap + 31) / 32; }
+__host__ __device__ __forceinline__ size_t topk_smem_bytes(int nb_cap) {
+  return ((nb_cap <= kSmemKeyBlocks ? (size_t)nb_cap : 0) + 2 * (size_t)bitmap_words(nb_cap)) *
+         sizeof(uint32_t);
+}
+
+template <bool kSmemKeys>
 __device__ void select_top_k(const SelectParams& p, int unit, int nb, const float* scores,
-                             uint32_t* keys, TopkShared& ts) {
+                             uint32_t* dyn, TopkShared& ts) {
+  uint32_t* keys = dyn;
+  uint32_t* tie_bits = dyn + (kSmemKeys ? p.nb_cap : 0);
+  uint32_t* pick_bits = tie_bits + bitmap_words(p.nb_cap);
+  auto key_at = [&](int i) -> uint32_t {
+    if constexpr (kSmemKeys) return keys[i];
+    else return float_order_key(__ldcg(scores + i));
+  };
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int budget = min(p.budget, nb);
   const int n_init = min(p.init, nb);
@@ -210,12 +231,12 @@ __device__ void select_top_k(const SelectParams& p, int unit, int nb, const floa
       const int i = base + u * kThreads + tid;
       if (i < nb) {
         nan_seen |= isnan(v[u]);
-        keys[i] = float_order_key(v[u]);
+        if constexpr (kSmemKeys) keys[i] = float_order_key(v[u]);
       }
     }
   }
   if (nan_seen) raise_status(p.status, SA_DEV_NONFINITE);
-  for (int w = tid; w < (nb + 31) / 32; w += kThreads) ts.tie_bits[w] = 0;
+  for (int w = tid; w < (nb + 31) / 32; w += kThreads) tie_bits[w] = 0;
   for (int i = tid; i < 256; i += kThreads) ts.hist[0][i] = 0;
   if (tid == 0) ts.ncand = 0;
   __syncthreads();
@@ -231,7 +252,7 @@ __device__ void select_top_k(const SelectParams& p, int unit, int nb, const floa
       if (bucket <= kTieMax) {
         // gather the members (in any order) and rank each among them
         for (int i = tid; i < nb; i += kThreads) {
-          const uint32_t k = keys[i];
+          const uint32_t k = key_at(i);
           if (!forced(i) && (k & mask) == prefix) {
             const int s = atomicAdd(&ts.ncand, 1);
             ts.cand_key[s] = k;
@@ -247,7 +268,7 @@ __device__ void select_top_k(const SelectParams& p, int unit, int nb, const floa
             const uint32_t kj = ts.cand_key[j];
             rank += kj > k || (kj == k && ts.cand_idx[j] < i);
           }
-          if (rank < remaining) atomicOr(&ts.tie_bits[i >> 5], 1u << (i & 31));
+          if (rank < remaining) atomicOr(&tie_bits[i >> 5], 1u << (i & 31));
         }
         __syncthreads();
         whole = false;
@@ -255,7 +276,7 @@ __device__ void select_top_k(const SelectParams& p, int unit, int nb, const floa
       }
       if (pass == 4) {
         // more than kTieMax equal keys: the first `remaining` by index
-        auto member = [&](int i) { return i < hi && !forced(i) && keys[i] == prefix; };
+        auto member = [&](int i) { return i < hi && !forced(i) && key_at(i) == prefix; };
         int n = 0;
         for (int base = lo; base < hi; base += 32) n += __popc(__ballot_sync(kFull, member(base + lane)));
         if (lane == 0) ts.warp_count[warp] = n;
@@ -267,7 +288,7 @@ __device__ void select_top_k(const SelectParams& p, int unit, int nb, const floa
           const uint32_t b = __ballot_sync(kFull, m);
           const uint32_t take =
               __ballot_sync(kFull, m && before + __popc(b & lanes_below) < remaining);
-          if (lane == 0) ts.tie_bits[base >> 5] = take;
+          if (lane == 0) tie_bits[base >> 5] = take;
           before += __popc(b);
         }
         __syncthreads();
@@ -281,7 +302,7 @@ __device__ void select_top_k(const SelectParams& p, int unit, int nb, const floa
       for (int i = tid; i < 256; i += kThreads) ts.hist[(pass + 1) & 1][i] = 0;
 #pragma unroll 4
       for (int i = tid; i < nb; i += kThreads) {
-        const uint32_t k = keys[i];
+        const uint32_t k = key_at(i);
         if (!forced(i) && (k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1);
       }
       __syncthreads();
@@ -326,15 +347,15 @@ __device__ void select_top_k(const SelectParams& p, int unit, int nb, const floa
     if (i >= hi) return false;
     if (forced(i)) return true;
     if (K == 0) return false;
-    const uint32_t km = keys[i] & mask;
+    const uint32_t km = key_at(i) & mask;
     if (km != prefix) return km > prefix;
-    return whole || (ts.tie_bits[i >> 5] >> (i & 31) & 1u) != 0u;
+    return whole || (tie_bits[i >> 5] >> (i & 31) & 1u) != 0u;
   };
   int n = 0;
 #pragma unroll 4
   for (int base = lo; base < hi; base += 32) {
     const uint32_t b = __ballot_sync(kFull, chosen(base + lane));
-    if (lane == 0) ts.pick_bits[base >> 5] = b;
+    if (lane == 0) pick_bits[base >> 5] = b;
     n += __popc(b);
   }
   if (lane == 0) ts.warp_count[warp] = n;
@@ -348,7 +369,7 @@ __device__ void select_top_k(const SelectParams& p, int unit, int nb, const floa
   }
   int32_t* ids = p.ids + (size_t)unit * p.budget;
   for (int base = lo; base < hi; base += 32) {
-    const uint32_t b = ts.pick_bits[base >> 5];
+    const uint32_t b = pick_bits[base >> 5];
     if (b >> lane & 1u) {
       const int at = pos + __popc(b & lanes_below);
       if (at < p.budget) ids[at] = base + lane;
@@ -440,7 +461,11 @@ __global__ void __launch_bounds__(kThreads, 10)
     if (!ts.last) return;
   }
 
-  select_top_k(p, unit, nb, scores, reinterpret_cast<uint32_t*>(smem), ts);
+  // q and dots are no longer needed: the top-k reuses the dynamic shared memory
+  if (p.nb_cap <= kSmemKeyBlocks)
+    select_top_k<true>(p, unit, nb, scores, reinterpret_cast<uint32_t*>(smem), ts);
+  else
+    select_top_k<false>(p, unit, nb, scores, reinterpret_cast<uint32_t*>(smem), ts);
 }
 
 }  // namespace
@@ -457,8 +482,8 @@ sa_status launch_select(const SelectParams& p, cudaStream_t stream) {
                   p.nb_cap % 4 == 0 && (reinterpret_cast<uintptr_t>(p.reps) & 15u) == 0;
   const int chunk = sub_chunks(p.group) * kWarpBlocks;
   const size_t smem =
-      std::max((((size_t)p.group * p.d + 3) & ~size_t(3)) + (size_t)p.group * chunk,
-               (size_t)p.nb_cap) * sizeof(float);
+      std::max(((((size_t)p.group * p.d + 3) & ~size_t(3)) + (size_t)p.group * chunk) * sizeof(float),
+               topk_smem_bytes(p.nb_cap));
   static int configured[kMaxDevices];
   const sa_status st =
       ensure_smem_limit((const void*)select_kernel, (int)std::max<size_t>(smem, 48 * 1024), configured);
