@@ -740,7 +740,7 @@ SA_API sa_status sa_ctx_create(const sa_ctx_config* config, sa_ctx** out) {
   if (st == SA_OK) st = dalloc(&d.query_ring, nsl * g.query_heads * kBlockTokens * kHeadDim);
   if (st == SA_OK) st = dalloc(&d.free_list, (size_t)g.pool_blocks);
   if (st == SA_OK) st = dalloc(&d.free_top, 1);
-  if (st == SA_OK) st = dalloc(&d.seal_counters, 1);
+  if (st == SA_OK) st = dalloc(&d.seal_counters, 2);
   if (st == SA_OK) st = dalloc(&d.status, 1);
   if (st == SA_OK) st = dalloc(&c->selected, nsl * c->n_sel_groups * g.budget_blocks);
   if (st == SA_OK) st = dalloc(&c->selected_count, nsl * c->n_sel_groups);
@@ -765,7 +765,7 @@ SA_API sa_status sa_ctx_create(const sa_ctx_config* config, sa_ctx** out) {
   if (st == SA_OK) {
     SA_CUDA_TRY(cudaMemset(d.pool, 0, (size_t)g.pool_blocks * kBlockTokens * row_elems * 2));
     SA_CUDA_TRY(cudaMemset(d.reps, 0, nsl * g.query_heads * kHeadDim * (size_t)c->table_pad * 4));
-    SA_CUDA_TRY(cudaMemset(d.seal_counters, 0, sizeof(int)));
+    SA_CUDA_TRY(cudaMemset(d.seal_counters, 0, 2 * sizeof(int)));
     SA_CUDA_TRY(cudaMemset(c->select_counters, 0, nsl * c->n_sel_groups * sizeof(int)));
     SA_CUDA_TRY(cudaMemset(c->attn_counters, 0, (size_t)units * sizeof(int)));
     SA_CUDA_TRY(cudaMemset(c->selected_count, 0, nsl * c->n_sel_groups * sizeof(int)));

@@ -159,6 +159,8 @@ __device__ __forceinline__ bool append_token(const CtxDev& c, int sl, const floa
                                              int qh0, int qh1, int tid, int nthreads) {
   const int tl = c.tail_len[sl];
   const int phys = c.tail_block[sl];
+  // a tail this token fills (or one already full) needs the seal's full pass
+  if (tid == 0 && tl >= kBlockTokens - 1) c.seal_counters[1] = 1;
   if (tl < 0 || tl >= kBlockTokens) {
     if (tid == 0) raise_status(c.status, SA_DEV_TAIL_FULL);
     return false;

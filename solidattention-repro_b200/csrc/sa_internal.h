@@ -68,7 +68,7 @@ struct CtxDev {
   float* query_ring;   // [num_sl][qh][32][128]
   int32_t* free_list;
   int32_t* free_top;
-  int* seal_counters;  // [1] arrivals of the seal kernel's CTAs
+  int* seal_counters;  // [0] arrivals of the seal kernel's CTAs; [1] 1 when an append filled a tail (or found it full)
   uint32_t* status;
   uint32_t* status_mirror;  // device-mapped host word the seal commit copies status to (nullable)
   int num_sl, qh, kv_heads;

@@ -384,6 +384,12 @@ __global__ void __launch_bounds__(kRepThreads) seal_kernel(const CtxDev c, int p
   __shared__ int last;
   pdl_launch_dependents();
   pdl_wait();  // the attention of this step still reads the tails
+  if (pending && __ldcg(c.seal_counters + 1) == 0) {
+    // The step's appends filled no tail (the fused append flags one that it
+    // fills or finds full): only the tail lengths move, by one CTA.
+    if (blockIdx.x == 0) seal_commit(c, pending);
+    return;
+  }
   const int items = c.qh * c.num_sl;
   // Most steps fill no tail: test all of this CTA's items in one round of
   // loads (one item per thread) before walking them one at a time.
@@ -403,7 +409,8 @@ __global__ void __launch_bounds__(kRepThreads) seal_kernel(const CtxDev c, int p
     last = atomicAdd(c.seal_counters, 1) == (int)gridDim.x - 1;
     if (last) {
       __threadfence();
-      *c.seal_counters = 0;
+      c.seal_counters[0] = 0;
+      c.seal_counters[1] = 0;  // every CTA has read the flag
     }
   }
   __syncthreads();

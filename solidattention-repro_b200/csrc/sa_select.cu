@@ -145,6 +145,7 @@ __device__ void raw_projections(const SelectParams& p, int sl, int g, float* qs,
   const int phys = c.tail_block[sl];
   const bool ok_tail = tl >= 0 && tl < kBlockTokens;
   const bool ok_block = phys >= 0 && phys < c.pool_blocks;
+  if (t == 0 && tl >= kBlockTokens - 1) c.seal_counters[1] = 1;  // the seal's full pass
   if (t == 0 && !ok_tail) raise_status(c.status, SA_DEV_TAIL_FULL);
   if (t == 0 && ok_tail && !ok_block) raise_status(c.status, SA_DEV_BAD_BLOCK);
   for (int j = 0; j < p.group; ++j) {
