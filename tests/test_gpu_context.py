@@ -466,6 +466,40 @@ def test_recorded_steps_replay_like_eager_steps(pkg, cuda):
         c.close()
 
 
+def test_stage_calls_match_the_fused_step_across_seals(pkg, cuda):
+    """The stage calls (sa_ctx_append, _select, _attend, _seal: the token is
+    counted at once and the seal runs its full pass) and the fused step (the
+    token pending until the seal, which commits alone unless the append
+    flagged a filled tail) give the same outputs and state bit for bit, also
+    when the two are interleaved on one context, across two seals."""
+    import dataclasses
+
+    from solidattention_repro_b200 import workloads
+
+    w = dataclasses.replace(workloads.CONFIGS["cfg2"], name="stage-step-test", layers=2,
+                            context_blocks=40, budget_blocks=12, hot_blocks=2)
+    steps = 70
+    fused, info = workloads.make_context(w, steps, cuda, seed=11)
+    mixed, _ = workloads.make_context(w, steps, cuda, seed=11)
+    q, kv = workloads.decode_inputs(w, info, steps, cuda, seed=11)
+    for s in range(steps):
+        want = fused.step(q[s], kv[s])
+        if s % 3 == 1:
+            got = mixed.step(q[s], kv[s])
+        else:
+            mixed.append(q[s], kv[s])
+            mixed.select(q[s])
+            got = mixed.attend(q[s])
+            mixed.seal()
+        assert torch.equal(got, want), s
+    for name in ("num_sealed", "tail_len", "tail_block", "generation", "selected", "reps", "table"):
+        assert torch.equal(getattr(mixed, name), getattr(fused, name)), name
+    assert (fused.generation.cpu().numpy() == 2).all()
+    for c in (fused, mixed):
+        assert c.status_bits() == 0
+        c.close()
+
+
 def test_slot_table_follows_the_selection_bit_exact(pkg, port, cuda):
     """sa_ctx_slot_correct over a decode loop: a resident window that starts
     empty and follows each step's selection equals the oracle's
