@@ -380,7 +380,9 @@ __device__ void seal_commit(const CtxDev& c, int pending) {
 // Grid-stride over (query head, sequence-layer) items: rebuild the
 // representative of every full tail; the last CTA to finish commits the
 // seals (an atomic arrival count, reset by that CTA; no spinning).
-__global__ void __launch_bounds__(kRepThreads) seal_kernel(const CtxDev c, int pending) {
+// Three CTAs per SM (74 KB of shared memory each, <= 85 registers): a full
+// seal of every head of every layer spreads over 444 CTAs.
+__global__ void __launch_bounds__(kRepThreads, 3) seal_kernel(const CtxDev c, int pending) {
   __shared__ int last;
   pdl_launch_dependents();
   pdl_wait();  // the attention of this step still reads the tails
@@ -508,9 +510,9 @@ sa_status launch_seal(const CtxDev& c, int pending, cudaStream_t stream, bool pd
   if (st != SA_OK) return st;
   if ((st = ensure_smem_limit((const void*)seal_kernel, (int)sizeof(RepSmem), g_seal_smem)) != SA_OK)
     return st;
-  // two CTAs per SM at most: an idle step (no full tail) costs one short wave
+  // three CTAs per SM at most; a step that fills no tail runs CTA 0 alone
   const int items = c.qh * c.num_sl;
-  const int grid = std::max(1, std::min(items, 2 * 148));
+  const int grid = std::max(1, std::min(items, 3 * 148));
   return cuda_status(launch_kernel(seal_kernel, dim3(grid), dim3(kRepThreads), sizeof(RepSmem),
                                    stream, pdl, c, pending),
                      "seal_kernel launch");
