@@ -132,12 +132,14 @@ def test_select_signed_zero_and_equal_scores(pkg, port, cuda):
     assert np.array_equal(ids.cpu().numpy(), want)
 
 
+@pytest.mark.parametrize("blocks", [1200, 5000])  # order keys in shared memory / from L2
 @pytest.mark.parametrize("case", ["crowded_bucket", "infinite_score", "two_values"])
-def test_select_top_k_adversarial_scores(pkg, port, cuda, case):
-    """Adversarial score sets for the radix top-k: two far outliers above 1200
-    near-equal scores, an infinite score, and scores of only two values."""
+def test_select_top_k_adversarial_scores(pkg, port, cuda, case, blocks):
+    """Adversarial score sets for the radix top-k: two far outliers above
+    near-equal scores, an infinite score, and scores of only two values (more
+    equal keys at the threshold than can be ranked directly)."""
     rng = np.random.default_rng({"crowded_bucket": 1, "infinite_score": 2, "two_values": 3}[case])
-    qh, blocks, budget = 4, 1200, 100
+    qh, budget = 4, 100
     q = rng.standard_normal((qh, 128), dtype=np.float32)
     base = rng.standard_normal((qh, 1, 128), dtype=np.float32)
     if case == "two_values":
