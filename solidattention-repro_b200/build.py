@@ -2,9 +2,8 @@
 
 Compiles every ``csrc/*.cu`` with nvcc for ``sm_100a`` only and links one
 shared library next to this file. cudart is linked statically (nvcc's
-default), so the library depends only on the driver at run time; the TMA
-descriptor encoder is fetched from the driver with cudaGetDriverEntryPoint.
-Object files go to ``<repo>/_build/`` and are rebuilt when a source or
+default), so the library depends only on the driver at run time. Object
+files go to ``<repo>/_build/`` and are rebuilt when a source or
 header is newer.
 """
 from __future__ import annotations

@@ -4,7 +4,6 @@
 // reference's error conditions, workspace plans,
 // the AcceleratorBackend-style handle (host buffers, event timings) and the
 // paged decode context (pool, free list, block tables, tails, seal).
-#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>

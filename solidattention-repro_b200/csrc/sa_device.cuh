@@ -3,7 +3,6 @@
 // scans, programmatic-launch hooks and the decode-tail append.
 #pragma once
 
-#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>

@@ -2,7 +2,6 @@
 // files and the C-ABI implementation (sa_api.cu). Not installed.
 #pragma once
 
-#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
