@@ -38,7 +38,9 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kLaneBlocks = 4;                      // consecutive blocks per lane
 constexpr int kWarpBlocks = 32 * kLaneBlocks;       // 128 blocks per warp pass
 constexpr int kMaxBlocks = 16384;
-constexpr int kDimUnroll = 8;
+constexpr int kDimUnroll = 8;        // dims in flight per warp: occupancy-bound grids
+constexpr int kDimUnrollDeep = 16;   // grids of at most kDeepGridCtas CTAs (latency-bound)
+constexpr int kDeepGridCtas = 5 * 148;
 constexpr unsigned kFull = 0xffffffffu;
 
 constexpr int kTieMax = kThreads;  // threshold buckets this small are ranked directly
@@ -83,6 +85,7 @@ __host__ __device__ __forceinline__ int sub_chunks(int group) { return kWarps / 
 // One head's dot products for the lane's 4 consecutive blocks b0..b0+3, in
 // the reference's order (sequential over dims, multiply and add rounded
 // separately).
+template <int DU>
 __device__ __forceinline__ void head_dots(const SelectParams& p, const float* rh, const float* qj,
                                           int b0, int nb, int vec, float (&dot)[kLaneBlocks]) {
 #pragma unroll
@@ -90,13 +93,13 @@ __device__ __forceinline__ void head_dots(const SelectParams& p, const float* rh
   if (vec) {
     const float* col = rh + b0;
     int dd = 0;
-    for (; dd + kDimUnroll <= p.d; dd += kDimUnroll) {
-      float4 r[kDimUnroll];
+    for (; dd + DU <= p.d; dd += DU) {
+      float4 r[DU];
 #pragma unroll
-      for (int u = 0; u < kDimUnroll; ++u)
+      for (int u = 0; u < DU; ++u)
         r[u] = ldg_no_l1(col + (size_t)(dd + u) * p.s_dim);
 #pragma unroll
-      for (int u = 0; u < kDimUnroll; ++u) {
+      for (int u = 0; u < DU; ++u) {
         const float q = qj[dd + u];
         dot[0] = dot_step(dot[0], q, r[u].x);
         dot[1] = dot_step(dot[1], q, r[u].y);
@@ -383,7 +386,11 @@ __device__ void select_top_k(const SelectParams& p, int unit, int nb, const floa
 // 10 resident CTAs per SM (48 registers): with the no-allocate loads the
 // select ran 100.3 us at cfg3 against 103.0 us at the compiler's 56 registers
 // (9 CTAs) and 104.4 / 118.5 us at 12 / 16 CTAs.
-__global__ void __launch_bounds__(kThreads, 10)
+// The deep variant keeps 16 dims (8 KB a warp) in flight for grids too small
+// to fill the SMs (cfg2: 448 CTAs), where only more bytes in flight per warp
+// hide the load latency.
+template <int DU, int kMinBlocks>
+__global__ void __launch_bounds__(kThreads, kMinBlocks)
     select_kernel(const SelectParams p, const int vec) {
   // dynamic shared memory: q [group][d], head dots [group][chunk], then (last
   // CTA) order keys [nb_cap]
@@ -427,7 +434,7 @@ __global__ void __launch_bounds__(kThreads, 10)
       float dot[kLaneBlocks] = {0.f, 0.f, 0.f, 0.f};
       if (b0 < nb) {
         const int h = g * p.group + j;
-        head_dots(p, p.reps + (size_t)sl * p.s_sl + (size_t)h * p.s_head, qs + j * p.d, b0, nb,
+        head_dots<DU>(p, p.reps + (size_t)sl * p.s_sl + (size_t)h * p.s_head, qs + j * p.d, b0, nb,
                   vec, dot);
       }
       *reinterpret_cast<float4*>(dots + (size_t)j * chunk + lb) =
@@ -485,13 +492,15 @@ sa_status launch_select(const SelectParams& p, cudaStream_t stream) {
   const size_t smem =
       std::max(((((size_t)p.group * p.d + 3) & ~size_t(3)) + (size_t)p.group * chunk) * sizeof(float),
                topk_smem_bytes(p.nb_cap));
-  static int configured[kMaxDevices];
-  const sa_status st =
-      ensure_smem_limit((const void*)select_kernel, (int)std::max<size_t>(smem, 48 * 1024), configured);
-  if (st != SA_OK) return st;
   const int nchunks = std::max(1, (p.nb_cap + chunk - 1) / chunk);
   const dim3 grid(nchunks, p.num_sl * p.n_groups);
-  const cudaError_t e = launch_kernel(select_kernel, grid, dim3(kThreads), smem, stream, p.pdl != 0, p, vec);
+  const bool deep = (long long)nchunks * p.num_sl * p.n_groups <= kDeepGridCtas;
+  auto kernel = deep ? select_kernel<kDimUnrollDeep, 5> : select_kernel<kDimUnroll, 10>;
+  static int configured[2][kMaxDevices];
+  const sa_status st = ensure_smem_limit((const void*)kernel, (int)std::max<size_t>(smem, 48 * 1024),
+                                         configured[deep ? 1 : 0]);
+  if (st != SA_OK) return st;
+  const cudaError_t e = launch_kernel(kernel, grid, dim3(kThreads), smem, stream, p.pdl != 0, p, vec);
   if (e != cudaSuccess) return cuda_status(e, "select_kernel launch");
   return cuda_status(cudaGetLastError(), "select_kernel launch");
 }
