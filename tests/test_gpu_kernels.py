@@ -89,7 +89,8 @@ def _reps_dim_major(reps_ref):
     (16, 16, 16, 4, 1, 1),       # the C2.1 shared mode
     (16, 2, 512, 64, 1, 4),      # per KV head, Qwen3-0.6B shape
     (32, 4, 1024, 128, 1, 4),    # per KV head, Qwen3-8B shape
-    (32, 4, 4096, 256, 1, 8),    # long context
+    (32, 4, 4096, 256, 1, 8),    # long context (a grid small enough for the deep variant)
+    (32, 4, 16384, 256, 1, 8),   # the maximum: 1024 CTAs, the occupancy-bound variant
     (4, 4, 1, 1, 0, 1),          # single block
     (8, 2, 50, 50, 1, 1),        # budget == blocks
     (8, 2, 50, 5, 2, 3),         # everything forced
