@@ -54,7 +54,7 @@ def parse_args():
     ap.add_argument("--kernel-iters", type=int, default=50)
     ap.add_argument("--launch", default="graph", choices=["graph", "eager"],
                     help="timed steps replayed from one recorded CUDA graph (sa_ctx_graph_*) "
-                         "or launched one call at a time; KV-head sharding always runs eager")
+                         "or launched one call at a time; KV-head sharding with the NCCL gather runs eager")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
@@ -344,7 +344,8 @@ def main():
         for s in range(args.warmup):
             step(s)
     ctx.sync()
-    use_graph = args.launch == "graph" and not heads_mode
+    # NCCL's all-gather stays outside graphs; the peer-memory gather records
+    use_graph = args.launch == "graph" and (not heads_mode or p2p)
     if use_graph:
         # record the K timed steps (nothing runs); the timed region replays them
         with torch.cuda.stream(stream), ctx.record():

@@ -408,7 +408,10 @@ SA_API sa_status sa_ctx_gather_buffer(sa_ctx* ctx, int32_t world, void** buf_out
 SA_API sa_status sa_ctx_gather_attach(sa_ctx* ctx, int32_t rank, void* const* peer_bufs);
 /* Enqueue the wait for the latest attention's outputs from every rank;
  * *gathered_out (nullable) = the slot holding them [seqs][layers][world*QH][D].
- * A wait that gives up sets SA_DEV_TIMEOUT in the status word. */
+ * A wait that gives up sets SA_DEV_TIMEOUT in the status word. The slot
+ * parity and the expected arrival count are kept on the device, so
+ * attention + wait pairs recorded with sa_ctx_graph_begin replay correctly
+ * (every attention must be followed by its wait before the next one). */
 SA_API sa_status sa_ctx_gather_wait(sa_ctx* ctx, void** gathered_out);
 /* CUDA IPC handle of a device allocation (SA_IPC_HANDLE_BYTES bytes), and
  * mapping / unmapping another process's allocation on `device`. */

@@ -120,7 +120,9 @@ struct sa_ctx {
   // decode-step graph: recorded between sa_ctx_graph_begin and _end
   bool recording = false;
   uint64_t launches_before_recording = 0;
-  uint64_t graph_launches = 0;  // kernel launches one replay issues
+  uint64_t gather_attends_before_recording = 0;
+  uint64_t graph_launches = 0;        // kernel launches one replay issues
+  uint64_t graph_gather_attends = 0;  // gathered attends one replay issues
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t graph_exec = nullptr;
 };
@@ -681,8 +683,10 @@ sa_status ctx_attend(sa_ctx* c, const float* query, void* out, int pending = 0,
     p.gather_peers = c->gather_peers;
     p.gather_world = c->gather_world;
     p.gather_rank = c->gather_rank;
-    p.gather_slot_bytes = (size_t)(c->gather_attends % 2) * c->gather_slot_bytes;
+    p.gather_slot_bytes = c->gather_slot_bytes;
     p.gather_counter_bytes = c->gather_counter_bytes;
+    p.gather_epoch = reinterpret_cast<const unsigned long long*>(c->gather_buf +
+                                                                 c->gather_counter_bytes + 8);
   }
   ++c->launches;
   const sa_status st = launch_attention(p, c->stream);
@@ -1069,6 +1073,7 @@ SA_API sa_status sa_ctx_graph_begin(sa_ctx* c) {
   SA_CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
   c->recording = true;
   c->launches_before_recording = c->launches;
+  c->gather_attends_before_recording = c->gather_attends;
   return SA_OK;
 }
 
@@ -1080,6 +1085,8 @@ SA_API sa_status sa_ctx_graph_end(sa_ctx* c) {
   // recorded calls launched nothing yet
   const uint64_t recorded = c->launches - c->launches_before_recording;
   c->launches = c->launches_before_recording;
+  const uint64_t recorded_attends = c->gather_attends - c->gather_attends_before_recording;
+  c->gather_attends = c->gather_attends_before_recording;
   cudaGraph_t graph = nullptr;
   SA_CUDA_TRY(cudaStreamEndCapture(c->stream, &graph));
   cudaGraphExec_t exec = nullptr;
@@ -1095,6 +1102,7 @@ SA_API sa_status sa_ctx_graph_end(sa_ctx* c) {
   c->graph = graph;
   c->graph_exec = exec;
   c->graph_launches = recorded;
+  c->graph_gather_attends = recorded_attends;
   return SA_OK;
 }
 
@@ -1105,6 +1113,7 @@ SA_API sa_status sa_ctx_graph_launch(sa_ctx* c) {
   DeviceGuard guard(c->cfg.device);
   SA_CUDA_TRY(cudaGraphLaunch(c->graph_exec, c->stream));
   c->launches += c->graph_launches;
+  c->gather_attends += c->graph_gather_attends;
   return SA_OK;
 }
 
@@ -1251,11 +1260,11 @@ SA_API sa_status sa_ctx_gather_wait(sa_ctx* c, void** gathered_out) {
   if (c->gather_attends == 0) return fail(SA_ERR_INVALID_ARG, "gather_wait: no gathered attend yet");
   DeviceGuard guard(c->cfg.device);
   const unsigned long long units = (unsigned long long)c->num_sl * c->cfg.kv_heads;
-  const unsigned long long expected = c->gather_attends * c->gather_world * units;
   ++c->launches;
   const sa_status st = launch_gather_wait(
       reinterpret_cast<const unsigned long long*>(c->gather_buf + c->gather_counter_bytes),
-      expected, c->dev.status, c->stream);
+      reinterpret_cast<unsigned long long*>(c->gather_buf + c->gather_counter_bytes + 8),
+      c->gather_world * units, c->dev.status, c->stream);
   if (st != SA_OK) return st;
   if (gathered_out)
     *gathered_out = c->gather_buf + ((c->gather_attends - 1) % 2) * c->gather_slot_bytes;

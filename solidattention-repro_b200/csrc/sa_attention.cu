@@ -273,7 +273,7 @@ __device__ __forceinline__ void gather_push(const AttnParams& p, AttnSmem<G>& s,
   const int chunks = G * kHeadDim * esz / 16;
   const int sl = u / p.kv_heads;
   const int kvh = u - sl * p.kv_heads;
-  const size_t off = p.gather_slot_bytes +
+  const size_t off = (size_t)(*p.gather_epoch & 1ull) * p.gather_slot_bytes +
                      (((size_t)sl * p.gather_world + p.gather_rank) * p.kv_heads + kvh) *
                          (size_t)(G * kHeadDim * esz);
   for (int i = vtid<virt_ctas<G>()>(); i < chunks * p.gather_world; i += kThreads) {
@@ -660,9 +660,15 @@ sa_status launch_g(const AttnParams& p, cudaStream_t stream) {
   return p.head_major ? launch_layout<G, true>(p, stream) : launch_layout<G, false>(p, stream);
 }
 
-__global__ void gather_wait_kernel(const unsigned long long* counter, unsigned long long expected,
-                                   uint32_t* status) {
+// Waits (bounded) until this rank's counter holds the arrivals of gather
+// epoch + 1, then advances the epoch: the next attention writes the other
+// slot. Epoch and expected count live on the device, so a recorded graph
+// replays them correctly.
+__global__ void gather_wait_kernel(const unsigned long long* counter, unsigned long long* epoch,
+                                   unsigned long long per_step, uint32_t* status) {
   if (threadIdx.x != 0) return;
+  const unsigned long long e = *reinterpret_cast<volatile unsigned long long*>(epoch);
+  const unsigned long long expected = (e + 1) * per_step;
   const long long start = clock64();
   for (;;) {
     unsigned long long v;
@@ -674,13 +680,14 @@ __global__ void gather_wait_kernel(const unsigned long long* counter, unsigned l
     }
     __nanosleep(256);
   }
+  *epoch = e + 1;
 }
 
 }  // namespace
 
-sa_status launch_gather_wait(const unsigned long long* counter, unsigned long long expected,
-                             uint32_t* status, cudaStream_t stream) {
-  gather_wait_kernel<<<1, 32, 0, stream>>>(counter, expected, status);
+sa_status launch_gather_wait(const unsigned long long* counter, unsigned long long* epoch,
+                             unsigned long long per_step, uint32_t* status, cudaStream_t stream) {
+  gather_wait_kernel<<<1, 32, 0, stream>>>(counter, epoch, per_step, status);
   return cuda_status(cudaGetLastError(), "gather_wait_kernel launch");
 }
 

@@ -114,15 +114,18 @@ struct AttnParams {
   int* counters;        // [units], zero between launches
   uint32_t* status;
   // KV-head-sharded gather over peer memory (gather_peers null = off): every
-  // unit's output also goes into the slot at gather_slot_bytes of every
-  // rank's buffer, laid out [sl][world * kv_heads][group][128] (the full
-  // head set, rank r's KV heads at [r * kv_heads, (r + 1) * kv_heads)),
-  // followed by one system-scope arrival on each rank's counter.
+  // unit's output also goes into slot (epoch & 1) of every rank's buffer
+  // (slots gather_slot_bytes apart), laid out [sl][world * kv_heads][group]
+  // [128] (the full head set, rank r's KV heads at [r * kv_heads,
+  // (r + 1) * kv_heads)), followed by one system-scope arrival on each rank's
+  // counter. The epoch is this rank's count of completed gathers, kept on the
+  // device so that a recorded graph replays correctly.
   void* const* gather_peers;      // device array [gather_world]
   int gather_world;
   int gather_rank;
   size_t gather_slot_bytes;
   size_t gather_counter_bytes;
+  const unsigned long long* gather_epoch;
 };
 
 // The persistent attention schedule: `ctas` CTAs, each owning a contiguous
@@ -138,8 +141,8 @@ size_t attention_scratch_bytes(const AttnPlan& plan, int units, int group);
 sa_status launch_attention(const AttnParams& p, cudaStream_t stream);
 // Waits (bounded, one thread) until *counter >= expected with system-scope
 // acquire; SA_DEV_TIMEOUT in *status when it gives up.
-sa_status launch_gather_wait(const unsigned long long* counter, unsigned long long expected,
-                             uint32_t* status, cudaStream_t stream);
+sa_status launch_gather_wait(const unsigned long long* counter, unsigned long long* epoch,
+                             unsigned long long per_step, uint32_t* status, cudaStream_t stream);
 
 // ---- selection (sa_select.cu) ----------------------------------------------------
 

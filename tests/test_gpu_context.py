@@ -304,6 +304,44 @@ def test_gather_over_peer_buffers_assembles_all_heads(pkg, cuda):
     full.close()
 
 
+def test_recorded_gather_steps_replay_like_eager_steps(pkg, cuda):
+    """The gather's slot parity and expected arrival count live on the device,
+    so attention + gather-wait pairs recorded into a graph replay correctly:
+    a one-rank gather (its own buffer, so no wait depends on another kernel)
+    replays five recorded steps, then an eager sixth step's wait finds that
+    step's output in the slot the host names."""
+    import dataclasses
+
+    from solidattention_repro_b200 import workloads
+
+    w = dataclasses.replace(workloads.CONFIGS["cfg3"], name="gather-graph-test", layers=2,
+                            context_blocks=48, budget_blocks=12, hot_blocks=2)
+    steps = 6
+    plain, info = workloads.make_context(w, steps, cuda, seed=12)
+    with torch.cuda.stream(torch.cuda.Stream(cuda)):
+        rec, _ = workloads.make_context(w, steps, cuda, seed=12)
+    q, kv = workloads.decode_inputs(w, info, steps, cuda, seed=12)
+    own, _ = rec.gather_buffer(1)
+    rec.gather_attach(0, [own])
+    outs = [rec.new_output() for _ in range(steps)]
+    torch.cuda.synchronize(cuda)
+    with rec.record():
+        for s in range(steps - 1):
+            rec.step(q[s], kv[s], outs[s])
+            rec.gather_wait(view=False)
+    rec.graph_launch()
+    rec.step(q[steps - 1], kv[steps - 1], outs[steps - 1])
+    gathered = rec.gather_wait()
+    rec.sync()
+    for s in range(steps):
+        want = plain.step(q[s], kv[s])
+        assert torch.equal(outs[s], want), s
+    assert torch.equal(gathered.reshape(outs[-1].shape), outs[-1])
+    for c in (rec, plain):
+        assert c.status_bits() == 0
+        c.close()
+
+
 def test_dense_audit_matches_float64_softmax(pkg, cuda):
     """sa_ctx_audit: per-block dense attention mass of each (seq-layer, KV
     head), averaged over its query heads, against a float64 restatement of
