@@ -342,6 +342,33 @@ def test_recorded_gather_steps_replay_like_eager_steps(pkg, cuda):
         c.close()
 
 
+def test_gather_wait_gives_up_and_reports_timeout(pkg, cuda):
+    """A gather wait whose arrivals never come (a second wait after a single
+    gathered attention: nothing will add the arrivals it expects) gives up at
+    its bounded limit (about a second) and reports SA_DEV_TIMEOUT in the
+    status word instead of hanging; the next synchronisation returns
+    SA_ERR_TIMEOUT."""
+    import dataclasses
+
+    from solidattention_repro_b200 import workloads
+
+    w = dataclasses.replace(workloads.CONFIGS["cfg3"], name="gather-timeout-test", layers=1,
+                            context_blocks=16, budget_blocks=8, hot_blocks=1)
+    ctx, info = workloads.make_context(w, 4, cuda, seed=13)
+    q, kv = workloads.decode_inputs(w, info, 1, cuda, seed=13)
+    own, _ = ctx.gather_buffer(1)
+    ctx.gather_attach(0, [own])
+    ctx.step(q[0], kv[0])
+    ctx.gather_wait(view=False)  # its arrivals are there
+    assert ctx.sync() == 0
+    ctx.gather_wait(view=False)  # expects the arrivals of an attention that never runs
+    with pytest.raises(pkg.SparseKVError) as e:
+        ctx.sync()
+    assert e.value.status == pkg.SA_ERR_TIMEOUT
+    assert ctx.status_bits() & pkg.SA_DEV_TIMEOUT
+    ctx.close()
+
+
 def test_dense_audit_matches_float64_softmax(pkg, cuda):
     """sa_ctx_audit: per-block dense attention mass of each (seq-layer, KV
     head), averaged over its query heads, against a float64 restatement of
