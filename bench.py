@@ -304,6 +304,7 @@ def main():
 
     total = args.steps + args.warmup
     e2e_steps = min(args.steps, 500)
+    dist_steps = min(args.steps, 100)  # per-step distribution pass (after the timed region)
     heads_mode = args.config == "cfg5" and world > 1
     if heads_mode:
         # KV-head sharding of one long sequence
@@ -316,7 +317,7 @@ def main():
     # table room for every append of the run: warmup + timed + e2e steps. The
     # context's stream is its own (a graph cannot record the default stream).
     with torch.cuda.stream(torch.cuda.Stream(dev)):
-        ctx, info = workloads.make_context(w, total + e2e_steps + 64, dev, seed=1,
+        ctx, info = workloads.make_context(w, total + e2e_steps + dist_steps + 64, dev, seed=1,
                                            kv_heads_slice=kv_slice, seq_offset=seq_offset)
     phase_bits = {}
     queries, kv_new = workloads.decode_inputs(w, info, total, dev, seed=1 + seq_offset,
@@ -377,6 +378,25 @@ def main():
     ms = max_over_ranks(ms_local)
     seqs_total = w.seqs if heads_mode else world * w.seqs
     steps_per_s = seqs_total * args.steps / (ms / 1000.0)
+
+    # ---- per-step distribution: one call per step, CUDA events between steps
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(dist_steps + 1)]
+    with torch.cuda.stream(stream):
+        evs[0].record(stream)
+        for i in range(dist_steps):
+            step(args.warmup + i)
+            evs[i + 1].record(stream)
+    evs[-1].synchronize()
+    per_step = sorted(evs[i].elapsed_time(evs[i + 1]) for i in range(dist_steps))
+    phase_bits["dist"] = ctx.status_bits()
+    ctx.sync()
+    barrier()
+
+    def pct(xs, q):
+        return xs[min(len(xs) - 1, int(round(q * (len(xs) - 1))))] if xs else None
+    step_dist = {"p10": pct(per_step, 0.1), "p50": pct(per_step, 0.5), "p90": pct(per_step, 0.9),
+                 "steps": dist_steps, "unit": "ms",
+                 "timing": "CUDA events between consecutive single-step calls, rank 0"}
 
     # ---- per-kernel roofline: each kernel alone, on its launch stream
     q_last = queries[total - 1]
@@ -450,9 +470,12 @@ def main():
     barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
+    e2e_times = []
     try:
         for _ in range(e2e_steps):
+            t_step = time.perf_counter()
             e2e_step()
+            e2e_times.append(1000.0 * (time.perf_counter() - t_step))
     finally:
         phase_bits["e2e"] = ctx.status_bits()
         if any(phase_bits.values()):
@@ -462,6 +485,9 @@ def main():
            "h2d_bytes_per_step": q_host.numel() * 4 + kv_host.numel() * 2,
            "d2h_bytes_per_step": out_host.numel() * out_host.element_size() + 4,
            "steps": e2e_steps, "timing": "host wall clock around synchronous calls, max over ranks"}
+    e2e_times.sort()
+    e2e["step_ms"] = {"p10": pct(e2e_times, 0.1), "p50": pct(e2e_times, 0.5),
+                      "p90": pct(e2e_times, 0.9), "rank": 0}
 
     # ---- selection quality of the last step (dense audit, not timed)
     from solidattention_repro_b200 import quality as quality_mod
@@ -517,6 +543,7 @@ def main():
                 "kv_dtype": "fp16", "accumulate": "fp32",
                 "launch": ("one CUDA graph of the timed steps (sa_ctx_graph_launch)" if use_graph
                            else "one sa_ctx_step call per step")},
+            "step_ms_distribution": step_dist,
             "selected_kv_gbs": attn_gbs, "selected_kv_frac": attn_gbs / hbm,
             # selected KV (16-token average tail) per GPU-step x per-GPU steps/s
             "step_selected_kv_gbs": w.selected_kv_bytes(16) * steps_per_s / world / 1e9,
