@@ -210,6 +210,59 @@ def run_cpu_baseline(ctx, w, q_step, n_layers_total, seconds, threads):
 
 # ---------------------------------------------------------------- reference arm
 
+def reference_shapes(pkg, dev) -> dict:
+    """The path's kernels at the shapes the reference published numbers for
+    (Qwen3-0.6B attention shape, 16 query / 8 KV heads, RTX 4080 Laptop):
+    C1.1 attention over 128 selected tokens (39.97 us kernel), C1.2 complete
+    backend call with host buffers (90.4 us wall), C2.1 selection over 16
+    blocks with budget 4 (14.6 us on the CPU). Device times are CUDA-event
+    means over 100 graph-replayed calls; the backend call is host wall time."""
+    import torch
+    rng = np.random.default_rng(7)
+    tokens, qh, kh = 128, 16, 8
+    kv = torch.from_numpy(rng.standard_normal(tokens * 2 * kh * 128).astype(np.float16)
+                          .view(np.int16)).to(dev)
+    q = torch.from_numpy(rng.standard_normal(qh * 128).astype(np.float32)).to(dev)
+    reps = torch.from_numpy(rng.standard_normal((qh, 16, 128)).astype(np.float32)).to(dev)
+
+    def graph_us(fn, calls=100):
+        side = torch.cuda.Stream(dev)
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn()
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            for _ in range(calls):
+                fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(side):
+            g.replay()
+            e0.record(side)
+            g.replay()
+            e1.record(side)
+        e1.synchronize()
+        return 1000.0 * e0.elapsed_time(e1) / calls
+
+    out = {"c1_1_attention_kernel_us": graph_us(lambda: pkg.attention(kv, q, tokens, qh, kh, 128)),
+           "c2_1_select_16_blocks_us": graph_us(
+               lambda: pkg.select_shared_blocks(q.view(qh, 128), reps, qh, 16, 128, 4, 1, 1))}
+    backend = pkg.Backend(dev.index)
+    kv_h, q_h = kv.cpu().numpy().view(np.uint16), q.cpu().numpy()
+    for _ in range(3):
+        backend.attention(kv_h, q_h, tokens, qh, kh, 128, 0.08838834764831845)
+    walls = []
+    for _ in range(200):
+        t0 = time.perf_counter()
+        backend.attention(kv_h, q_h, tokens, qh, kh, 128, 0.08838834764831845)
+        walls.append(1e6 * (time.perf_counter() - t0))
+    backend.close()
+    out["c1_2_backend_call_wall_us"] = statistics.median(walls)
+    out["reference_published_us"] = {"c1_1_attention_kernel": 39.97, "c1_2_backend_call_wall": 90.433,
+                                     "c2_1_select_cpu": 14.579, "hardware": "RTX 4080 Laptop / i9-14900HX"}
+    return out
+
+
 def reference_arm(args, w, rank):
     """The reference's CPU implementation of the path on host cores (no GPU work)."""
     if rank != 0:
@@ -519,6 +572,7 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = run_cpu_baseline(ctx, w, q_last, w.layers, args.cpu_seconds, os.cpu_count() or 1)
+    ref_shapes = reference_shapes(pkg, dev) if rank == 0 and world == 1 else None
 
     if rank == 0:
         line = {
@@ -558,6 +612,7 @@ def main():
                            "frac": sel_gbs / hbm}},
             "quality": qual,
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": gpu_launches,
+            "reference_shapes": ref_shapes,
             "device_status_bits": phase_bits,
             "clocks": clock_info,
         }

@@ -98,6 +98,8 @@ struct sa_ctx {
   int32_t* selected_count = nullptr;
   float* scores = nullptr;
   int* select_counters = nullptr;
+  char* select_split = nullptr;  // head-split scratch of groups above four heads
+  size_t select_split_bytes = 0;
   float* attn_partial = nullptr;
   int* attn_counters = nullptr;
   AttnPlan attn_plan{};
@@ -225,7 +227,8 @@ SA_API size_t sa_select_workspace_size(size_t query_heads, size_t group, size_t 
   if (group == 0 || query_heads % group != 0) return 0;
   const size_t n_groups = query_heads / group;
   const size_t cap = (blocks + 3) & ~size_t(3);
-  return n_groups * cap * sizeof(float) + n_groups * sizeof(int) + 256;
+  const size_t base = (n_groups * cap * sizeof(float) + n_groups * sizeof(int) + 255) & ~size_t(255);
+  return base + select_split_scratch_bytes((int)n_groups, (int)group, (int)cap) + 256;
 }
 
 SA_API sa_status sa_select_blocks(const float* query, const float* reps, int64_t stride_head,
@@ -275,6 +278,12 @@ SA_API sa_status sa_select_blocks(const float* query, const float* reps, int64_t
   // A caller's reps extent along blocks is `blocks`: keep vector loads inside it.
   p.nb_cap = (stride_block == 1 && blocks % 4 != 0) ? (int)blocks : cap;
   SA_CUDA_TRY(cudaMemsetAsync(p.counters, 0, n_groups * sizeof(int), s));
+  // groups of more than four heads: the head split's dots and chunk counters
+  const size_t base = (n_groups * cap * sizeof(float) + n_groups * sizeof(int) + 255) & ~size_t(255);
+  select_bind_split_scratch(p, ws + base, (int)n_groups);
+  if (p.chunk_counters)
+    SA_CUDA_TRY(cudaMemsetAsync(p.chunk_counters, 0,
+                                n_groups * select_max_chunks(p.group, p.nb_cap) * sizeof(int), s));
   const int row = p.nb_cap;
   sa_status st = launch_select(p, s);
   if (st != SA_OK) return st;
@@ -631,6 +640,7 @@ SelectParams select_params(sa_ctx* c, const float* query) {
   p.scores = c->scores;
   p.counters = c->select_counters;
   p.status = c->dev.status;
+  select_bind_split_scratch(p, c->select_split, c->num_sl * c->n_sel_groups);
   return p;
 }
 
@@ -749,6 +759,9 @@ SA_API sa_status sa_ctx_create(const sa_ctx_config* config, sa_ctx** out) {
   if (st == SA_OK) st = dalloc(&c->selected_count, nsl * c->n_sel_groups);
   if (st == SA_OK) st = dalloc(&c->scores, nsl * c->n_sel_groups * (size_t)c->table_pad);
   if (st == SA_OK) st = dalloc(&c->select_counters, nsl * c->n_sel_groups);
+  c->select_split_bytes =
+      select_split_scratch_bytes((int)(nsl * c->n_sel_groups), g.select_group, c->table_pad);
+  if (st == SA_OK && c->select_split_bytes) st = dalloc(&c->select_split, c->select_split_bytes);
   if (st == SA_OK)
     st = dalloc(reinterpret_cast<char**>(&c->attn_partial),
                 attention_scratch_bytes(c->attn_plan, units, c->group));
@@ -770,6 +783,7 @@ SA_API sa_status sa_ctx_create(const sa_ctx_config* config, sa_ctx** out) {
     SA_CUDA_TRY(cudaMemset(d.reps, 0, nsl * g.query_heads * kHeadDim * (size_t)c->table_pad * 4));
     SA_CUDA_TRY(cudaMemset(d.seal_counters, 0, 2 * sizeof(int)));
     SA_CUDA_TRY(cudaMemset(c->select_counters, 0, nsl * c->n_sel_groups * sizeof(int)));
+    if (c->select_split) SA_CUDA_TRY(cudaMemset(c->select_split, 0, c->select_split_bytes));
     SA_CUDA_TRY(cudaMemset(c->attn_counters, 0, (size_t)units * sizeof(int)));
     SA_CUDA_TRY(cudaMemset(c->selected_count, 0, nsl * c->n_sel_groups * sizeof(int)));
     st = sa_ctx_reset(c);
@@ -798,7 +812,7 @@ SA_API sa_status sa_ctx_destroy(sa_ctx* c) {
   CtxDev& d = c->dev;
   void* ptrs[] = {d.pool, d.reps, d.table, d.num_sealed, d.tail_block, d.tail_len, d.generation,
                   d.query_ring, d.free_list, d.free_top, d.seal_counters, d.status, c->selected,
-                  c->selected_count, c->scores, c->select_counters, c->attn_partial,
+                  c->selected_count, c->scores, c->select_counters, c->select_split, c->attn_partial,
                   c->attn_counters, c->d_query, c->d_qt, c->d_kv_new, c->d_out, c->gather_buf,
                   c->gather_peers};
   for (void* p : ptrs) cudaFree(p);

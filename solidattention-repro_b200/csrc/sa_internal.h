@@ -160,6 +160,13 @@ struct SelectParams {
   int32_t* counts;    // [num_sl][n_groups] (nullable)
   float* scores;      // [num_sl][n_groups][nb_cap]
   int* counters;      // [num_sl][n_groups], zero between launches
+  // Groups of more than four heads are split over CTAs, four heads each
+  // (select_head_splits): each writes its heads' dot products to
+  // head_dots [num_sl * n_groups][group][nb_cap] and the last of a chunk's
+  // CTAs (chunk_counters [num_sl * n_groups][select_max_chunks], zero between
+  // launches) adds them in head order.
+  float* head_dots;
+  int* chunk_counters;
   uint32_t* status;
   // Fused append (append_kv null = off): the first CTA of each unit writes
   // the step's K/V of the group's KV heads into row tail_len of the
@@ -186,6 +193,13 @@ struct SelectParams {
 };
 
 int select_max_blocks();
+// CTAs a unit's heads are split over (1 for groups of at most four heads),
+// chunks of a unit of nb_cap blocks, and the scratch bytes of the split
+// (head_dots, then chunk_counters; 0 when there is no split).
+int select_head_splits(int group);
+int select_max_chunks(int group, int nb_cap);
+size_t select_split_scratch_bytes(int units, int group, int nb_cap);
+void select_bind_split_scratch(SelectParams& p, void* scratch, int units);
 sa_status launch_select(const SelectParams& p, cudaStream_t stream);
 
 // ---- representatives, append, seal (sa_lifecycle.cu) ------------------------------

@@ -77,6 +77,13 @@ __device__ __forceinline__ float dot_step(float acc, float q, float r) {
   return __fadd_rn(acc, __fmul_rn(q, r));
 }
 
+// CTAs a unit's heads are split over: groups of more than four heads (the
+// reference's shared mode puts all query heads in one group) give each CTA
+// four heads, one per warp, instead of walking them in sequence.
+__host__ __device__ __forceinline__ int head_splits(int group) {
+  return group > kWarps ? (group + kWarps - 1) / kWarps : 1;
+}
+
 // Warps per head and block sub-chunks of a CTA: with fewer than four heads
 // per group the spare warps take further 128-block sub-chunks.
 __host__ __device__ __forceinline__ int heads_per_pass(int group) { return group < kWarps ? group : kWarps; }
@@ -407,18 +414,22 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
   const int chunk = sub * kWarpBlocks;
   const int nchunks = max(1, (nb + chunk - 1) / chunk);
   if ((int)blockIdx.x >= nchunks) return;
+  // heads [hb, hb + nh) of the group are this CTA's
+  const int hsplit = head_splits(p.group);
+  const int hb = (int)blockIdx.z * kWarps;
+  const int nh = hsplit > 1 ? min(kWarps, p.group - hb) : p.group;
   float* qs = smem;
-  float* dots = smem + ((p.group * p.d + 3) & ~3);  // 16-byte aligned
+  float* dots = smem + ((nh * p.d + 3) & ~3);  // 16-byte aligned
 
-  if (p.append_kv && blockIdx.x == 0) {
+  if (p.append_kv && blockIdx.x == 0 && blockIdx.z == 0) {
     // fused decode-tail append of this group's heads (tail_len unchanged)
     const int q0 = g * p.group;
     const int per_kv = p.qh / p.append_ctx.kv_heads;
     append_token(p.append_ctx, sl, p.query, p.append_kv, p.append_kv_fp32, q0 / per_kv,
                  (q0 + p.group) / per_kv, q0, q0 + p.group, threadIdx.x, kThreads);
   }
-  const float* qsrc = p.query + ((size_t)sl * p.qh + (size_t)g * p.group) * p.d;
-  for (int i = threadIdx.x; i < p.group * p.d; i += kThreads) qs[i] = qsrc[i];
+  const float* qsrc = p.query + ((size_t)sl * p.qh + (size_t)g * p.group + hb) * p.d;
+  for (int i = threadIdx.x; i < nh * p.d; i += kThreads) qs[i] = qsrc[i];
   __syncthreads();
   if (p.raw_k) raw_projections(p, sl, g, qs, dots);
 
@@ -430,10 +441,10 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
   if (sc < sub) {
     const int lb = sc * kWarpBlocks + lane * kLaneBlocks;  // chunk-local first block
     const int b0 = cbase + lb;
-    for (int j = warp % hp; j < p.group; j += hp) {
+    for (int j = warp % hp; j < nh; j += hp) {
       float dot[kLaneBlocks] = {0.f, 0.f, 0.f, 0.f};
       if (b0 < nb) {
-        const int h = g * p.group + j;
+        const int h = g * p.group + hb + j;
         head_dots<DU>(p, p.reps + (size_t)sl * p.s_sl + (size_t)h * p.s_head, qs + j * p.d, b0, nb,
                   vec, dot);
       }
@@ -445,12 +456,43 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
   // ---- block scores: sum over the group's heads in head order ----
   float* scores = p.scores + (size_t)unit * p.nb_cap;
   const float divisor = (float)p.group;
-  for (int lb = threadIdx.x; lb < chunk; lb += kThreads) {
-    const int b = cbase + lb;
-    if (b >= nb) break;
-    float score = 0.f;
-    for (int j = 0; j < p.group; ++j) score = __fadd_rn(score, __fdiv_rn(dots[(size_t)j * chunk + lb], divisor));
-    scores[b] = score;
+  if (hsplit == 1) {
+    for (int lb = threadIdx.x; lb < chunk; lb += kThreads) {
+      const int b = cbase + lb;
+      if (b >= nb) break;
+      float score = 0.f;
+      for (int j = 0; j < p.group; ++j)
+        score = __fadd_rn(score, __fdiv_rn(dots[(size_t)j * chunk + lb], divisor));
+      scores[b] = score;
+    }
+  } else {
+    // publish this CTA's heads; the chunk's last CTA adds all heads in order
+    float* hd = p.head_dots + (size_t)unit * p.group * p.nb_cap;
+    for (int i = threadIdx.x; i < nh * chunk; i += kThreads) {
+      const int j = i / chunk, lb = i - j * chunk, b = cbase + lb;
+      if (b < nb) hd[(size_t)(hb + j) * p.nb_cap + b] = dots[(size_t)j * chunk + lb];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      // the barrier orders the CTA's dot stores before this fence
+      __threadfence();
+      int* cc = p.chunk_counters + (size_t)unit * ((p.nb_cap + chunk - 1) / chunk) + blockIdx.x;
+      ts.last = atomicAdd(cc, 1) == hsplit - 1;
+      if (ts.last) {
+        __threadfence();
+        *cc = 0;
+      }
+    }
+    __syncthreads();
+    if (!ts.last) return;
+    for (int lb = threadIdx.x; lb < chunk; lb += kThreads) {
+      const int b = cbase + lb;
+      if (b >= nb) break;
+      float score = 0.f;
+      for (int j = 0; j < p.group; ++j)
+        score = __fadd_rn(score, __fdiv_rn(__ldcg(hd + (size_t)j * p.nb_cap + b), divisor));
+      scores[b] = score;
+    }
   }
 
   // ---- the last CTA of this (sl, group) selects ----
@@ -480,6 +522,26 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
 
 int select_max_blocks() { return kMaxBlocks; }
 
+int select_head_splits(int group) { return head_splits(group); }
+
+int select_max_chunks(int group, int nb_cap) {
+  const int chunk = sub_chunks(group) * kWarpBlocks;
+  return std::max(1, (nb_cap + chunk - 1) / chunk);
+}
+
+size_t select_split_scratch_bytes(int units, int group, int nb_cap) {
+  if (head_splits(group) == 1) return 0;
+  const size_t dots = ((size_t)units * group * nb_cap * sizeof(float) + 255) & ~size_t(255);
+  return dots + (size_t)units * select_max_chunks(group, nb_cap) * sizeof(int);
+}
+
+void select_bind_split_scratch(SelectParams& p, void* scratch, int units) {
+  if (head_splits(p.group) == 1 || !scratch) return;
+  const size_t dots = ((size_t)units * p.group * p.nb_cap * sizeof(float) + 255) & ~size_t(255);
+  p.head_dots = static_cast<float*>(scratch);
+  p.chunk_counters = reinterpret_cast<int*>(static_cast<char*>(scratch) + dots);
+}
+
 sa_status launch_select(const SelectParams& p, cudaStream_t stream) {
   if (p.num_sl <= 0 || p.n_groups <= 0) return SA_OK;
   if (p.nb_cap > kMaxBlocks)
@@ -489,12 +551,18 @@ sa_status launch_select(const SelectParams& p, cudaStream_t stream) {
   const int vec = p.s_block == 1 && p.s_dim % 4 == 0 && p.s_head % 4 == 0 && p.s_sl % 4 == 0 &&
                   p.nb_cap % 4 == 0 && (reinterpret_cast<uintptr_t>(p.reps) & 15u) == 0;
   const int chunk = sub_chunks(p.group) * kWarpBlocks;
+  const int hsplit = head_splits(p.group);
+  if (hsplit > 1 && (!p.head_dots || !p.chunk_counters))
+    return fail(SA_ERR_INVALID_ARG, "select: groups of more than 4 heads need the split scratch");
+  if (hsplit > 1 && p.raw_k)
+    return fail(SA_ERR_UNSUPPORTED, "select: raw projections need groups of at most 4 heads");
+  const size_t nh = hsplit > 1 ? (size_t)kWarps : (size_t)p.group;
   const size_t smem =
-      std::max(((((size_t)p.group * p.d + 3) & ~size_t(3)) + (size_t)p.group * chunk) * sizeof(float),
+      std::max((((nh * p.d + 3) & ~size_t(3)) + nh * chunk) * sizeof(float),
                topk_smem_bytes(p.nb_cap));
   const int nchunks = std::max(1, (p.nb_cap + chunk - 1) / chunk);
-  const dim3 grid(nchunks, p.num_sl * p.n_groups);
-  const bool deep = (long long)nchunks * p.num_sl * p.n_groups <= kDeepGridCtas;
+  const dim3 grid(nchunks, p.num_sl * p.n_groups, hsplit);
+  const bool deep = (long long)nchunks * p.num_sl * p.n_groups * hsplit <= kDeepGridCtas;
   auto kernel = deep ? select_kernel<kDimUnrollDeep, 5> : select_kernel<kDimUnroll, 10>;
   static int configured[2][kMaxDevices];
   const sa_status st = ensure_smem_limit((const void*)kernel, (int)std::max<size_t>(smem, 48 * 1024),
