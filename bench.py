@@ -216,7 +216,8 @@ def reference_shapes(pkg, dev) -> dict:
     C1.1 attention over 128 selected tokens (39.97 us kernel), C1.2 complete
     backend call with host buffers (90.4 us wall), C2.1 selection over 16
     blocks with budget 4 (14.6 us on the CPU). Device times are CUDA-event
-    means over 100 graph-replayed calls; the backend call is host wall time."""
+    means over 100 graph-replayed calls; the backend call is the median host
+    wall time of a call from Python with pinned host buffers."""
     import torch
     rng = np.random.default_rng(7)
     tokens, qh, kh = 128, 16, 8
@@ -248,7 +249,12 @@ def reference_shapes(pkg, dev) -> dict:
            "c2_1_select_16_blocks_us": graph_us(
                lambda: pkg.select_shared_blocks(q.view(qh, 128), reps, qh, 16, 128, 4, 1, 1))}
     backend = pkg.Backend(dev.index)
-    kv_h, q_h = kv.cpu().numpy().view(np.uint16), q.cpu().numpy()
+    # pinned host buffers, as the reference's allocate_host gives its drivers
+    kv_pin = torch.empty(kv.shape, dtype=torch.int16, pin_memory=True)
+    q_pin = torch.empty(q.shape, dtype=torch.float32, pin_memory=True)
+    kv_pin.copy_(kv.cpu())
+    q_pin.copy_(q.cpu())
+    kv_h, q_h = kv_pin.numpy().view(np.uint16), q_pin.numpy()
     for _ in range(3):
         backend.attention(kv_h, q_h, tokens, qh, kh, 128, 0.08838834764831845)
     walls = []

@@ -127,7 +127,7 @@ def select_shared_blocks(query: torch.Tensor, representatives: torch.Tensor, que
     ids = torch.empty(n_groups, max(budget_blocks, 1), dtype=torch.int32, device=dev)
     scores = torch.empty(n_groups, max(blocks, 1), dtype=torch.float32, device=dev)
     ws_bytes = lib.sa_select_workspace_size(query_heads, group, blocks) if group else 0
-    ws = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)  # the call zeroes its counters
     check(lib.sa_select_blocks(_dev_ptr(query, torch.float32, "query"),
                                _dev_ptr(representatives, torch.float32, "representatives"),
                                *strides, query_heads, group, blocks, head_dim, budget_blocks,
