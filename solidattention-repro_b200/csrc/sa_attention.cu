@@ -697,9 +697,11 @@ AttnPlan attention_plan(int units, int slots_per_unit, int group) {
   const long long total = U * E;
   const long long wave = (long long)kSms * (group <= 4 ? 2 : 1);  // resident CTAs
   // Estimated time of a CTA count, in stage times (two slots per stage): the
-  // CTAs run in ceil(C / wave) waves; a segment end (the 8-warp merge) costs
-  // about three stages, and a unit split over n CTAs 2 + n/8 more (its
-  // partials and their merge by the last CTA).
+  // CTAs run in ceil(C / wave) waves; a segment end (the 8-warp merge and the
+  // next unit's start) costs about five stages, and a unit split over n CTAs
+  // 2 + n/8 more (its partials and their merge by the last CTA). Five, not
+  // three: at cfg2 (224 units of 65 slots) one whole unit per CTA ran the
+  // attention in 44.2 us, against 47.9 us for 296 CTAs splitting units.
   auto cost = [&](long long C) -> double {
     if (C < 1 || C > total) return 1e30;
     const long long per = (total + C - 1) / C;
@@ -722,7 +724,7 @@ AttnPlan attention_plan(int units, int slots_per_unit, int group) {
     if (segs > kMaxSegments) return 1e30;
     const long long waves = (C + wave - 1) / wave;
     const double parts = split ? (double)((E + per - 1) / per + 1) : 0.0;
-    return (double)waves * (double)(stages + 3 * segs) + (split ? 2.0 + parts / 8.0 : 0.0);
+    return (double)waves * (double)(stages + 5 * segs) + (split ? 2.0 + parts / 8.0 : 0.0);
   };
   long long best = 0;
   double best_cost = 1e30;
