@@ -125,7 +125,11 @@ _LIB = None
 
 
 def load() -> C.CDLL:
-    """The loaded library with prototypes set; raises if it is not built."""
+    """The loaded library with prototypes set; raises if it is not built.
+
+    SA_B200_LIB names another build of the same library (a copy built
+    elsewhere, e.g. with different nvcc flags); it must export every symbol
+    below, and nothing else is loaded in its place."""
     global _LIB
     if _LIB is not None:
         return _LIB
