@@ -71,6 +71,8 @@ PROTOTYPES = {
     "sa_attention_workspace_size": (_sz, [_sz, _sz, _sz]),
     "sa_attention_packed": (C.c_int, [_vp, _vp, _sz, _sz, _sz, _sz, C.c_float, _vp, C.c_int,
                                       _vp, _sz, _vp]),
+    "sa_attention_packed_noalloc": (C.c_int, [_vp, _vp, _sz, _sz, _sz, _sz, C.c_float, _vp,
+                                              C.c_int, _vp]),
     "sa_select_workspace_size": (_sz, [_sz, _sz, _sz]),
     "sa_select_blocks": (C.c_int, [_vp, _vp, _i64, _i64, _i64, _sz, _sz, _sz, _sz, _sz, _sz,
                                    _sz, _vp, _vp, _vp, _sz, _vp]),

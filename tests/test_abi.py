@@ -38,6 +38,32 @@ def test_library_exports_every_declared_symbol(pkg):
     assert not missing, missing
 
 
+def test_python_binding_declares_every_symbol():
+    """The ctypes binding sets a prototype for every entry point the header declares."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("_sa_lib", ROOT / "solidattention-repro_b200" / "_lib.py")
+    lib = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(lib)
+    missing = [n for n in declared_symbols() if n not in lib.PROTOTYPES]
+    assert not missing, missing
+
+
+def test_shared_mode_workspace_includes_the_head_split(pkg):
+    """Groups above four heads split over CTAs need dot and counter scratch."""
+    lib = pkg.load()
+    per_kv_head = lib.sa_select_workspace_size(16, 4, 1024)
+    shared = lib.sa_select_workspace_size(16, 16, 1024)
+    # the shared group's 16 heads x 1024 blocks of FP32 dots
+    assert shared - per_kv_head >= 16 * 1024 * 4 - 4 * 1024 * 4
+
+
+def test_graph_calls_reject_a_null_context(pkg):
+    lib = pkg.load()
+    for fn in (lib.sa_ctx_graph_begin, lib.sa_ctx_graph_end, lib.sa_ctx_graph_launch):
+        assert fn(None) == pkg.SA_ERR_INVALID_ARG
+
+
 def test_host_only_calls(pkg):
     lib = pkg.load()
     assert lib.sa_version().decode().startswith("sa_b200")
