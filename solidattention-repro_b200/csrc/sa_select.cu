@@ -226,6 +226,29 @@ __device__ void select_top_k(const SelectParams& p, int unit, int nb, const floa
   const int seg = (nb + kThreads - 1) / kThreads * 32;
   const int lo = warp * seg, hi = min(nb, lo + seg);
   const uint32_t lanes_below = (1u << lane) - 1u;
+  // f(i, key) for this thread's blocks i = tid, tid + kThreads, ... < nb;
+  // keys recomputed from L2 arrive kKeyBatch loads at a time
+  constexpr int kKeyBatch = 16;
+  auto for_keys = [&](auto&& f) {
+    if constexpr (kSmemKeys) {
+#pragma unroll 4
+      for (int i = tid; i < nb; i += kThreads) f(i, keys[i]);
+    } else {
+      for (int base = 0; base < nb; base += kThreads * kKeyBatch) {
+        uint32_t k[kKeyBatch];
+#pragma unroll
+        for (int u = 0; u < kKeyBatch; ++u) {
+          const int i = base + u * kThreads + tid;
+          k[u] = i < nb ? float_order_key(__ldcg(scores + i)) : 0u;
+        }
+#pragma unroll
+        for (int u = 0; u < kKeyBatch; ++u) {
+          const int i = base + u * kThreads + tid;
+          if (i < nb) f(i, k[u]);
+        }
+      }
+    }
+  };
 
   // keys, with every load of a batch in flight at once
   constexpr int kLoadBatch = 16;
@@ -262,14 +285,13 @@ __device__ void select_top_k(const SelectParams& p, int unit, int nb, const floa
       if (bucket == remaining) break;
       if (bucket <= kTieMax) {
         // gather the members (in any order) and rank each among them
-        for (int i = tid; i < nb; i += kThreads) {
-          const uint32_t k = key_at(i);
+        for_keys([&](int i, uint32_t k) {
           if (!forced(i) && (k & mask) == prefix) {
             const int s = atomicAdd(&ts.ncand, 1);
             ts.cand_key[s] = k;
             ts.cand_idx[s] = i;
           }
-        }
+        });
         __syncthreads();
         if (tid < bucket) {
           const uint32_t k = ts.cand_key[tid];
@@ -311,11 +333,9 @@ __device__ void select_top_k(const SelectParams& p, int unit, int nb, const floa
       const int shift = 24 - 8 * pass;
       int* hist = ts.hist[pass & 1];
       for (int i = tid; i < 256; i += kThreads) ts.hist[(pass + 1) & 1][i] = 0;
-#pragma unroll 4
-      for (int i = tid; i < nb; i += kThreads) {
-        const uint32_t k = key_at(i);
+      for_keys([&](int i, uint32_t k) {
         if (!forced(i) && (k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1);
-      }
+      });
       __syncthreads();
       if (warp == 0) {
         // digits in descending order: lane l holds digits 255 - 8l - j
@@ -354,20 +374,31 @@ __device__ void select_top_k(const SelectParams& p, int unit, int nb, const floa
   }
 
   // chosen blocks in index order
-  auto chosen = [&](int i) {
+  auto chosen = [&](int i, uint32_t key) {
     if (i >= hi) return false;
     if (forced(i)) return true;
     if (K == 0) return false;
-    const uint32_t km = key_at(i) & mask;
+    const uint32_t km = key & mask;
     if (km != prefix) return km > prefix;
     return whole || (tie_bits[i >> 5] >> (i & 31) & 1u) != 0u;
   };
   int n = 0;
-#pragma unroll 4
-  for (int base = lo; base < hi; base += 32) {
-    const uint32_t b = __ballot_sync(kFull, chosen(base + lane));
-    if (lane == 0) pick_bits[base >> 5] = b;
-    n += __popc(b);
+  constexpr int kWordBatch = kSmemKeys ? 1 : 8;  // 32-block words whose keys load together
+  for (int base0 = lo; base0 < hi; base0 += 32 * kWordBatch) {
+    uint32_t k[kWordBatch];
+#pragma unroll
+    for (int u = 0; u < kWordBatch; ++u) {
+      const int i = base0 + 32 * u + lane;
+      k[u] = i < hi ? key_at(i) : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < kWordBatch; ++u) {
+      const int base = base0 + 32 * u;
+      if (base >= hi) break;
+      const uint32_t b = __ballot_sync(kFull, chosen(base + lane, k[u]));
+      if (lane == 0) pick_bits[base >> 5] = b;
+      n += __popc(b);
+    }
   }
   if (lane == 0) ts.warp_count[warp] = n;
   __syncthreads();
