@@ -1,32 +1,42 @@
 #!/usr/bin/env python
 """Benchmark of the B200 sparse-KV decode path (one JSON line on rank 0).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg3] [--impl ours|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg3]
+                  [--impl ours|reference] [--shard auto|heads|seqs]
 
 A step is one decode step of the workload: for every (sequence, layer)
 append the token's K/V, score + select blocks per KV head, attend over the
 selected blocks plus the open tail, and seal the tail when it holds 32
-tokens. The default workload is the path's target configuration: Qwen3-8B
-shape (32 query / 8 KV heads, head_dim 128, 36 layers), 32K context (1024
-blocks), 4096-token budget (1 init + 4 local + 123 dynamic blocks). At N > 1
-each rank decodes its own sequences (sequence sharding by global batch index,
-no data-path collective): weak scaling; value = all ranks' sequence-steps /
-max time. `--config cfg5` (one 128K-context sequence) shards the KV heads
-instead: rank r holds KH/N heads of every layer, and each step ends with an
-NCCL all-gather of the per-head outputs: strong scaling.
+tokens (rebuilding the sealed block's representative). The default workload
+is the path's target configuration: Qwen3-8B shape (32 query / 8 KV heads,
+head_dim 128, 36 layers), one sequence of 32K context (1024 blocks), 4096-token
+budget (1 init + 4 local + 123 dynamic blocks). Every open tail starts with
+the tokens that make the last timed step a seal step, so the timed window
+always holds at least one seal and representative rebuild.
+
+Multi-GPU (N > 1, one process per GPU): a single-sequence config is split by
+KV head (rank r holds KH/N heads of every layer), and each step's per-head
+outputs are gathered by the attention kernel's peer-memory stores over NVLink
+(--gather nccl: an NCCL all-gather after the step): strong scaling, value =
+steps/s of the one sequence. A batched config (cfg4) is split by sequence
+(no data-path collective): weak scaling. With --shard heads at N > 1 the line
+also carries `replicas`: every rank decoding its own whole sequence.
 
 `value` is device-timed with inputs resident in HBM, the timed steps replayed
-from one recorded CUDA graph (`--launch eager` issues one call per step); `e2e` runs the same
-steps through the public host-buffer call (sa_ctx_step_host: H2D of the
-step's query + new K/V, step, D2H of the output, synchronize).
-`--impl reference` times the reference's own CPU implementation (the C++
-selector + attention compiled from its sources, oracle/_ref) on the host's
-cores over a bounded sample of the same workload.
+from one recorded CUDA graph (`--launch eager` issues one call per step); `e2e`
+runs the same steps through the public host-buffer call (sa_ctx_step_host:
+H2D of the step's query + new K/V, step, D2H of the output, synchronize).
+`--impl reference` times the reference's own CPU implementation (its C++
+selector, packed gather, attention and seal-time representative rebuild,
+compiled from its sources into oracle/_ref) on the host's cores, on the same
+seeded inputs (generated on GPU 0 with the same generator calls, then
+copied to the host), over a bounded sample of the step's units.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import re
 import statistics
@@ -42,6 +52,7 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "sparse decode attn steps/s + selected-KV HBM GB/s (% of peak) at 1/2/4/8 B200"
 FALLBACK_HBM_GBS = 6650.0
+SEED = 1
 
 
 def parse_args():
@@ -51,16 +62,24 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--config", default="cfg3", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--shard", default="auto", choices=["auto", "heads", "seqs"],
+                    help="N > 1: split one sequence's KV heads over the ranks (heads; the "
+                         "single-sequence configs' default) or give each rank its own "
+                         "sequences (seqs; the batched config's default)")
     ap.add_argument("--kernel-iters", type=int, default=50)
     ap.add_argument("--launch", default="graph", choices=["graph", "eager"],
                     help="timed steps replayed from one recorded CUDA graph (sa_ctx_graph_*) "
-                         "or launched one call at a time; KV-head sharding with the NCCL gather runs eager")
+                         "or launched one call at a time; the NCCL gather runs eager")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-replicas", action="store_true",
+                    help="skip the per-rank whole-sequence replica run of a KV-head split")
+    ap.add_argument("--cpu-seconds", type=float, default=8.0,
+                    help="host time of each cpu_baseline timing (1 thread, all cores)")
+    ap.add_argument("--ref-seconds", type=float, default=40.0,
+                    help="--impl reference: host time budget of each of its two timings")
     ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
-                    help="KV-head sharding (cfg5, N > 1): gather the per-head outputs with "
-                         "peer-memory stores from the attention kernel (p2p) or an NCCL "
-                         "all-gather after it (nccl)")
+                    help="KV-head split: gather the per-head outputs with peer-memory stores "
+                         "from the attention kernel (p2p) or an NCCL all-gather after it")
     ap.add_argument("--layers", type=int, default=None,
                     help="override the workload's layer count (small profiling cases)")
     return ap.parse_args()
@@ -144,7 +163,49 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
-# ------------------------------------------------------------ CPU baseline
+# ------------------------------------------------------------ layout, config
+
+def job_layout(args, w, world: int, rank: int):
+    """(shard, kv_heads_slice, seq_offset) of this rank: 'single' at N = 1,
+    'heads' (one sequence's KV heads split over the ranks) or 'seqs' (each
+    rank its own sequences of the batch)."""
+    from solidattention_repro_b200 import sharding
+
+    if world == 1:
+        return "single", None, 0
+    shard = args.shard
+    if shard == "auto":
+        shard = "seqs" if w.batch > 1 else "heads"
+    if shard == "heads":
+        return "heads", sharding.shard_kv_heads(w.kv_heads, world, rank), 0
+    return "seqs", None, rank * w.seqs
+
+
+def job_config(args, w, world: int, shard: str, initial_tail: int) -> dict:
+    """The workload both arms run (identical keys and values in both lines)."""
+    seqs_total = w.seqs * (world if shard == "seqs" else 1)
+    if shard == "heads":
+        par = (f"kv-head-split x{world}, outputs gathered every step by "
+               + ("the attention kernel's peer-memory stores (NVLink P2P)" if args.gather == "p2p"
+                  else "an NCCL all-gather"))
+    elif shard == "seqs":
+        par = f"sequence-split x{world}, no data-path collective"
+    else:
+        par = "single"
+    return {
+        "workload": w.name, "layers": w.layers, "query_heads": w.query_heads,
+        "kv_heads": w.kv_heads, "head_dim": 128, "context_tokens": w.context_blocks * 32,
+        "context_min_tokens": (w.context_min_blocks or w.context_blocks) * 32,
+        "budget_blocks": w.budget_blocks, "init_blocks": w.init_blocks,
+        "local_blocks": w.local_blocks, "hot_blocks": w.hot_blocks, "seqs": seqs_total,
+        "tail_tokens_at_start": initial_tail, "parallelism": par,
+        "l2": "inputs larger than L2: each step reads its selected KV and all representatives "
+              f"({(w.selected_kv_bytes() + w.rep_bytes()) / 1e9:.2f} GB per step at full context)",
+        "kv_dtype": "fp16", "accumulate": "fp32", "seed": SEED,
+    }
+
+
+# ------------------------------------------------------------ CPU path (reference's own C++)
 
 def cpu_lib():
     import oracle
@@ -153,62 +214,273 @@ def cpu_lib():
     return (ref, "reference") if ref is not None else (oracle.port(), "port")
 
 
-def cpu_step_sample(lib, pool_host, table_host, reps_host, q_host, tail_host, tail_len, w,
-                    nb, threads):
-    ids, out = lib.sparse_step(pool_host, table_host, reps_host, q_host, tail_host, tail_len,
-                               w.query_heads, w.kv_heads, 128, 32, nb,
-                               min(w.budget_blocks, nb), w.init_blocks, w.local_blocks,
-                               np.float32(1.0) / np.sqrt(np.float32(128)), threads)
-    return ids, out
+class HostSeqLayer:
+    """One (sequence, layer) of the decode state on the host, in the
+    reference's token-major layout: sealed blocks in logical order followed
+    by the open tail block, representatives [QH][nb][D], the tail's queries."""
+
+    def __init__(self, blocks, nb, reps, tail_len, ring, extra_blocks: int):
+        kh_row = blocks.shape[1:]
+        self.blocks = np.zeros((nb + 1 + extra_blocks,) + tuple(kh_row), np.uint16)
+        self.blocks[:nb + 1] = blocks[:nb + 1]
+        self.nb = nb
+        self.reps = np.ascontiguousarray(reps, np.float32)
+        self.tail_len = tail_len
+        self.ring = np.ascontiguousarray(ring, np.float32)  # [QH][32][D]
+
+    def append(self, q, kv_row):
+        """The step's token: its K/V row into the tail block, its queries into
+        the ring (a host copy; the reference's store write is host I/O)."""
+        self.blocks[self.nb, self.tail_len] = kv_row
+        self.ring[:, self.tail_len] = q
+        self.tail_len += 1
+
+    def seal(self, lib, qh, kh):
+        """The tail holds 32 tokens: rebuild its representative with the
+        reference's build over the tail's own queries (T = 32), as the online
+        seal does; returns the rebuild's host seconds."""
+        t0 = time.perf_counter()
+        values, _ = lib.build_representatives(self.ring, self.blocks[self.nb], 32, qh, kh, 128, 32,
+                                              32, 4)
+        dt = time.perf_counter() - t0
+        self.reps = np.ascontiguousarray(np.concatenate([self.reps, values], axis=1))
+        self.nb += 1
+        self.tail_len = 0
+        return dt
 
 
-def host_sample_from_ctx(ctx, layers):
-    """Copy the sampled layers' sealed blocks, tails, tables and reps to host."""
-    import torch
+class UnitSet:
+    """ctypes Unit array over (state, KV head) pairs in (state, head) order,
+    with the id and output arrays it points to (kept alive here); the states'
+    blocks and `queries` [n_states][QH][D] stay owned by the caller."""
 
+    def __init__(self, oracle_mod, states, queries, kh, grp, budget, n=None):
+        pairs = [(i, h) for i in range(len(states)) for h in range(kh)]
+        self.pairs = pairs[:n] if n else pairs
+        self.states = states
+        self.units = (oracle_mod.Unit * len(self.pairs))()
+        self.ids = np.zeros((len(self.pairs), budget), np.int64)
+        self.out = np.zeros((len(self.pairs), grp, 128), np.float32)
+        for k, (i, h) in enumerate(self.pairs):
+            u = self.units[k]
+            u.blocks = states[i].blocks.ctypes.data
+            u.query = queries[i].ctypes.data
+            u.kv_head = h
+            u.ids_out = self.ids[k].ctypes.data
+            u.out = self.out[k].ctypes.data
+
+    def refresh(self):
+        """Point every unit at its state's current block count, tail length
+        and representatives."""
+        for k, (i, _) in enumerate(self.pairs):
+            st = self.states[i]
+            self.units[k].reps = st.reps.ctypes.data
+            self.units[k].nb = st.nb
+            self.units[k].tail_len = st.tail_len
+
+    def run(self, lib, w, qh, kh, threads) -> float:
+        """Host seconds of the reference path over these units."""
+        t0 = time.perf_counter()
+        lib.sparse_units(self.units, qh, kh, 128, w.budget_blocks, w.init_blocks, w.local_blocks,
+                         np.float32(1.0) / np.sqrt(np.float32(128)), threads)
+        return time.perf_counter() - t0
+
+
+def host_states_from_ctx(ctx, sls):
+    """HostSeqLayer copies of the context's current state for sequence-layers
+    `sls`: sealed blocks through the table, the open tail, representatives,
+    the query ring."""
     nb_all = ctx.num_sealed.cpu().numpy()
     tables = ctx.table.cpu().numpy()
     tails = ctx.tail_block.cpu().numpy()
-    tail_len = int(ctx.tail_len.cpu().numpy()[layers[0]])
-    nb = int(nb_all[layers[0]])
-    pools, table_rows, tail_rows, reps = [], [], [], []
-    for i, l in enumerate(layers):
-        phys = np.concatenate([tables[l, :nb], tails[l:l + 1]]).astype(np.int64)
-        pools.append(ctx.read_blocks(phys).cpu().numpy().view(np.uint16))
-        table_rows.append(np.arange(nb, dtype=np.int32) + i * (nb + 1))
-        tail_rows.append(i * (nb + 1) + nb)
-        reps.append(ctx.reps[l, :, :, :nb].permute(0, 2, 1).contiguous().cpu().numpy())
-    return (np.concatenate(pools), np.stack(table_rows), np.stack(reps),
-            np.asarray(tail_rows, np.int32), tail_len, nb)
+    tl_all = ctx.tail_len.cpu().numpy()
+    states = []
+    for sl in sls:
+        nb = int(nb_all[sl])
+        phys = np.concatenate([tables[sl, :nb], tails[sl:sl + 1]]).astype(np.int64)
+        blocks = ctx.read_blocks(phys).cpu().numpy().view(np.uint16)
+        reps = ctx.reps[sl, :, :, :nb].permute(0, 2, 1).contiguous().cpu().numpy()
+        ring = ctx.query_ring[sl].cpu().numpy()
+        states.append(HostSeqLayer(blocks, nb, reps, int(tl_all[sl]), ring, 0))
+    return states
 
 
-def run_cpu_baseline(ctx, w, q_step, n_layers_total, seconds, threads):
-    """Time the reference CPU path (selection per KV head + gather + attention)
-    over a bounded sample of layers of the current decode step; extrapolate."""
+def run_cpu_baseline(ctx, w, q_step, seconds, cores):
+    """The reference's CPU path (its selector per KV head, packed gather and
+    attention, compiled from its sources) on the GPU context's current state
+    and query: all cores over 4 sequence-layers, one thread over 4 units;
+    each extrapolated to the whole step. Also checks that the CPU's selected
+    ids equal the GPU's on the sampled units."""
+    import oracle
+
     lib, kind = cpu_lib()
-    layers = list(range(min(4, n_layers_total)))
+    sls = list(range(min(4, ctx.num_sl)))
     ctx.select(q_step)
     sel = ctx.selected.cpu().numpy()
-    pool_h, table_h, reps_h, tail_h, tail_len, nb = host_sample_from_ctx(ctx, layers)
-    q_h = q_step.reshape(-1, w.query_heads, 128)[layers].cpu().numpy()
-    times, ids = [], None
-    t_end = time.perf_counter() + seconds
-    while time.perf_counter() < t_end or len(times) < 2:
-        t0 = time.perf_counter()
-        ids, _ = cpu_step_sample(lib, pool_h, table_h, reps_h, q_h, tail_h, tail_len, w, nb, threads)
-        times.append(time.perf_counter() - t0)
-    per_sample = statistics.median(times)
-    steps_per_s = 1.0 / (per_sample * n_layers_total / len(layers))
-    eff = min(w.budget_blocks, nb)
-    match = bool(np.array_equal(ids, sel[layers][:, :, :eff].astype(np.int64)))
-    return {"value": steps_per_s, "unit": "steps/s", "cores": threads, "kind": kind,
-            "sample": f"{len(layers)} of {n_layers_total} layers of one decode step "
-                      f"(select per KV head + packed gather + attention, {nb} sealed blocks, "
-                      f"tail {tail_len}), median of {len(times)} runs, extrapolated to all layers",
-            "ids_match_gpu": match}
+    counts = ctx.selected_count.cpu().numpy()
+    states = host_states_from_ctx(ctx, sls)
+    q = q_step.reshape(ctx.num_sl, ctx.qh, 128)[sls].cpu().numpy()
+    qs = [np.ascontiguousarray(q[i]) for i in range(len(sls))]
+    grp = ctx.qh // ctx.kh
+    units_total = ctx.num_sl * ctx.kh
+    result = {"unit": "steps/s", "kind": kind, "cores": cores}
+    match = True
+    for label, threads, n in (("all", cores, None), ("1thread", 1, 4)):
+        us = UnitSet(oracle, states, qs, ctx.kh, grp, w.budget_blocks, n)
+        us.refresh()
+        times = []
+        t_end = time.perf_counter() + seconds
+        while time.perf_counter() < t_end or len(times) < 2:
+            times.append(us.run(lib, w, ctx.qh, ctx.kh, threads))
+        per_step = statistics.median(times) * units_total / len(us.pairs)
+        result[f"steps_per_s_{label}"] = 1.0 / per_step
+        result[f"runs_{label}"] = len(times)
+        ids = us.ids
+        for k, (i, h) in enumerate(us.pairs):
+            sl = sls[i]
+            g = h * ctx.n_groups // ctx.kh
+            c = int(counts[sl, g])
+            match &= bool(np.array_equal(ids[k, :c], sel[sl, g, :c].astype(np.int64)))
+    result["value"] = result["steps_per_s_all"]
+    result["ids_match_gpu"] = match
+    result["sample"] = (f"the live decode state of {len(sls)} of {ctx.num_sl} sequence-layers "
+                        f"({states[0].nb} sealed blocks, tail {states[0].tail_len}): all {cores} "
+                        f"threads over their {len(sls) * ctx.kh} (sequence-layer, KV head) units, "
+                        f"1 thread over 4 units; medians, extrapolated to the {units_total} units "
+                        f"of a step")
+    return result
 
 
-# ---------------------------------------------------------------- reference arm
+def reference_arm(args, w, rank, world):
+    """The reference's own CPU implementation on identical seeded inputs.
+
+    The workload's values come from the same generator calls as the GPU arm
+    (torch's CUDA generator on GPU 0, then copied to the host: the data
+    generation is not timed and runs none of this repository's kernels).
+    Representatives are built on the host by the reference's own function.
+    Every step then runs, on host cores, the reference path of a sample of
+    the step's (sequence, layer, KV head) units: append the token, select
+    per KV head, packed gather, attention, and on the seal step the
+    representative rebuild; all cores over the sampled sequence-layers and
+    one thread over a subset sized to the time budget, each extrapolated to
+    the whole step."""
+    if rank != 0:
+        return
+    import torch
+
+    import oracle
+    from solidattention_repro_b200 import workloads
+
+    shard, _, _ = job_layout(args, w, world, 0)
+    K, W = args.steps, args.warmup
+    total = K + W
+    t0 = workloads.tail_for_seal_at_end(K, W)
+    lib, kind = cpu_lib()
+    cores = os.cpu_count() or 1
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    qh, kh, grp = w.query_heads, w.kv_heads, w.group
+    # sampled sequence-layers: spread over the layers (and over the first
+    # rank's sequences for a batch), fewer for long contexts (host memory)
+    n_sl = max(1, min(4, (4 * 1024) // max(1, w.context_blocks)))
+    layers = sorted({round(x) for x in np.linspace(0, w.layers - 1, n_sl)})
+    pairs = [(s % w.seqs, l) for s, l in zip(range(len(layers)), layers)]
+    setup0 = time.perf_counter()
+    info = {"layer_ids": list(range(w.layers))}
+    q_base = torch.stack([workloads.base_queries(w, SEED, s, dev) for s in range(w.seqs)])
+    info["q_base"] = q_base
+    queries, kv_new = workloads.decode_inputs(w, info, total, dev, seed=SEED)
+    states, step_q, step_kv = [], [], []
+    extra = total // 32 + 2
+    for s, layer in pairs:
+        nb = w.sequence_blocks(s)
+        hot = workloads.hot_blocks(w, SEED, s)
+        kv = workloads.prompt_kv(w, SEED, s, layer, q_base[s, layer], hot[layer], dev)
+        kv_h = kv.view(torch.int16).cpu().numpy().view(np.uint16).reshape(nb, 32, 2, kh, 128)
+        del kv
+        pq = workloads.prompt_queries(w, SEED, s, layer, dev).cpu().numpy()
+        reps = lib.build_reps_per_block(pq, kv_h, nb, qh, kh, 128, 32, 4, cores)
+        del pq
+        blocks = np.zeros((nb + 1, 32, 2, kh, 128), np.uint16)
+        blocks[:nb] = kv_h
+        ring = np.zeros((qh, 32, 128), np.float32)
+        st = HostSeqLayer(blocks, nb, reps, 0, ring, extra)
+        if t0:
+            tq, tkv = workloads.tail_tokens(w, SEED, s, q_base[s], t0, dev)
+            tq = tq[:, layer].cpu().numpy()
+            tkv = tkv[:, layer].view(torch.int16).cpu().numpy().view(np.uint16)
+            for t in range(t0):
+                st.append(tq[t], tkv[t])
+        states.append(st)
+        step_q.append(queries[:, s, layer].cpu().numpy())
+        step_kv.append(kv_new[:, s, layer].view(torch.int16).cpu().numpy().view(np.uint16))
+    del queries, kv_new
+    torch.cuda.synchronize(dev)
+    setup_s = time.perf_counter() - setup0
+    qbuf = [np.zeros((qh, 128), np.float32) for _ in states]
+    set_all = UnitSet(oracle, states, qbuf, kh, grp, w.budget_blocks)
+    units_step = w.seqs * w.layers * kh            # units of one sequence-step, per sequence
+    sl_step = w.layers                             # sequence-layers per sequence-step
+    # one thread over a subset sized to the time budget: calibrate one unit
+    for i, st in enumerate(states):
+        qbuf[i][:] = step_q[i][0]
+    set_cal = UnitSet(oracle, states, qbuf, kh, grp, w.budget_blocks, 1)
+    set_cal.refresh()
+    unit_s = min(set_cal.run(lib, w, qh, kh, 1) for _ in range(2))
+    n1 = int(max(1, min(len(set_all.pairs), args.ref_seconds / max(1e-6, total * unit_s))))
+    set_one = UnitSet(oracle, states, qbuf, kh, grp, w.budget_blocks, n1)
+    t_all, t_one, t_seal = [], [], []
+    for i in range(total):
+        for k, st in enumerate(states):
+            st.append(step_q[k][i], step_kv[k][i])
+            qbuf[k][:] = step_q[k][i]
+        set_all.refresh()
+        set_one.refresh()
+        a = set_all.run(lib, w, qh, kh, cores)
+        b = set_one.run(lib, w, qh, kh, 1)
+        seal = 0.0
+        if states[0].tail_len == 32:
+            seal = statistics.mean(st.seal(lib, qh, kh) for st in states)
+        if i >= W:
+            t_all.append(a)
+            t_one.append(b)
+            t_seal.append(seal)
+    # per sequence-step: unit work scaled from the sample, seal rebuilds of
+    # every sequence-layer (spread over the cores in the all-core figure)
+    per_units_all = statistics.mean(t_all) * (w.layers * kh) / len(set_all.pairs)
+    per_units_one = statistics.mean(t_one) * (w.layers * kh) / len(set_one.pairs)
+    seal_mean = statistics.mean(t_seal) if t_seal else 0.0
+    step_all = per_units_all + seal_mean * sl_step / min(cores, sl_step)
+    step_one = per_units_one + seal_mean * sl_step
+    value = 1.0 / step_all
+    seals = workloads.seal_steps(t0, W, K)
+    sample = (f"per step, {len(states)} sequence-layers of the workload (layers {layers}, "
+              f"{states[0].nb} sealed blocks at the end): append, select per KV head, packed "
+              f"gather and attention of their {len(set_all.pairs)} units on all {cores} threads and of "
+              f"{n1} of them on 1 thread, and the reference's representative rebuild on the "
+              f"{seals} seal step(s); extrapolated to the {units_step} units and {sl_step} "
+              f"sequence-layers of a sequence-step; inputs generated on GPU 0 by the GPU arm's "
+              f"generator calls ({setup_s:.1f} s of setup, not timed)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "steps/s",
+        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": 1000.0 / value,
+        "higher_is_better": True, "scaling": "weak" if shard == "seqs" else "strong",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded FP16 N(0,1) KV with planted hot blocks, seeded queries "
+                "(identical to the GPU arm's)",
+        "config": job_config(args, w, world, shard, t0),
+        "seals_in_timed_region": seals,
+        "cpu_baseline": {"value": value, "unit": "steps/s", "cores": cores, "kind": kind,
+                         "sample": sample, "steps_per_s_all": value,
+                         "steps_per_s_1thread": 1.0 / step_one, "threads_all": cores},
+        "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+
+# ---------------------------------------------------------------- reference shapes
 
 def reference_shapes(pkg, dev) -> dict:
     """The path's kernels at the shapes the reference published numbers for
@@ -269,80 +541,77 @@ def reference_shapes(pkg, dev) -> dict:
     return out
 
 
-def reference_arm(args, w, rank):
-    """The reference's CPU implementation of the path on host cores (no GPU work)."""
-    if rank != 0:
-        return
-    lib, kind = cpu_lib()
-    threads = os.cpu_count() or 1
-    rng = np.random.default_rng(1234)
-    total = args.steps + args.warmup
-    n_sample = 2 if total > 40 else 4
-    n_sample = min(n_sample, w.layers)
-    nb = w.context_blocks
-    if w.context_min_blocks:
-        nb = int(round(np.mean([w.sequence_blocks(b) for b in range(w.batch)])))
-    tail_len = 16
-    tv = 2 * w.kv_heads * 128
-    pool = (rng.standard_normal((n_sample * (nb + 1) * 32 * tv,), dtype=np.float32)
-            .astype(np.float16).view(np.uint16))
-    table = np.stack([np.arange(nb, dtype=np.int32) + i * (nb + 1) for i in range(n_sample)])
-    tails = np.asarray([i * (nb + 1) + nb for i in range(n_sample)], np.int32)
-    reps = (rng.standard_normal((n_sample, w.query_heads, nb, 128), dtype=np.float32) * 0.5
-            ).astype(np.float16).astype(np.float32)
-    q = rng.standard_normal((n_sample, w.query_heads, 128), dtype=np.float32
-                            ).astype(np.float16).astype(np.float32)
-    for _ in range(args.warmup):
-        cpu_step_sample(lib, pool, table, reps, q, tails, tail_len, w, nb, threads)
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        cpu_step_sample(lib, pool, table, reps, q, tails, tail_len, w, nb, threads)
-        times.append(time.perf_counter() - t0)
-    per_layer = sum(times) / len(times) / n_sample
-    value = 1.0 / (per_layer * w.layers)
-    sample = (f"{n_sample} of {w.layers} layers per step (select per KV head + packed gather + "
-              f"attention over {min(w.budget_blocks, nb)} blocks + {tail_len}-token tail), "
-              f"extrapolated to all layers")
-    line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "steps/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 / value, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": w.name, "layers": w.layers, "query_heads": w.query_heads,
-                   "kv_heads": w.kv_heads, "head_dim": 128, "context_tokens": nb * 32,
-                   "budget_blocks": w.budget_blocks},
-        "cpu_baseline": {"value": value, "unit": "steps/s", "cores": threads, "kind": kind,
-                         "sample": sample},
-        "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
-
-
 # ---------------------------------------------------------------- our arm
 
-def main():
-    args = parse_args()
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+def timed_steps(ctx, step, first, count, use_graph, stream, barrier):
+    """Records steps [first, first + count) (when use_graph) and times them
+    on the device: (ms, launches of this repository's kernels, clocks)."""
+    import torch
 
-    import __graft_entry__
+    if use_graph:
+        # record the timed steps (nothing runs); the timed region replays them
+        with torch.cuda.stream(stream), ctx.record():
+            for s in range(first, first + count):
+                step(s)
+    barrier()
+    torch.cuda.synchronize()
+    launches0 = ctx.launches
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.wait_first()  # the sampler is running before the region starts
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        if use_graph:
+            ctx.graph_launch()
+        else:
+            for s in range(first, first + count):
+                step(s)
+        end.record(stream)
+    end.synchronize()
+    clock_info = clocks.stop()
+    return start.elapsed_time(end), ctx.launches - launches0, clock_info
 
-    pkg = __graft_entry__.load_package()
+
+def replica_run(args, w, dev, rank, world, barrier, max_over_ranks):
+    """Every rank decodes its own whole sequence (global index = rank), no
+    collective: the weak-scaling counterpart of a KV-head split."""
+    import torch
+
     from solidattention_repro_b200 import workloads
 
-    w = workloads.CONFIGS[args.config]
-    if args.layers:
-        import dataclasses
-        w = dataclasses.replace(w, layers=args.layers, name=f"{w.name}-{args.layers}layers")
-    if args.impl == "reference":
-        reference_arm(args, w, rank)
-        return
+    K, W = args.steps, args.warmup
+    t0 = workloads.tail_for_seal_at_end(K, W)
+    with torch.cuda.stream(torch.cuda.Stream(dev)):
+        ctx, info = workloads.make_context(w, K + W + 64, dev, seed=SEED, seq_offset=rank,
+                                           initial_tail=t0)
+    queries, kv_new = workloads.decode_inputs(w, info, K + W, dev, seed=SEED + rank)
+    out = ctx.new_output()
 
+    def step(s):
+        ctx.step(queries[s], kv_new[s], out)
+
+    with torch.cuda.stream(ctx.stream):
+        for s in range(W):
+            step(s)
+    ctx.sync()
+    ms, launches, _ = timed_steps(ctx, step, W, K, args.launch == "graph", ctx.stream, barrier)
+    bits = ctx.status_bits()
+    ctx.close()
+    ms = max_over_ranks(ms)
+    return {"value": world * K / (ms / 1000.0), "unit": "sequence-steps/s",
+            "ms_per_step": ms / K, "scaling": "weak", "gpu_launches": launches,
+            "device_status_bits": bits,
+            "layout": f"each of the {world} ranks decodes its own whole sequence (global "
+                      f"index = rank), all KV heads, no collective"}
+
+
+def our_arm(args, w, rank, world, local_rank, pkg):
     import torch
     import torch.distributed as dist
+
+    from solidattention_repro_b200 import quality as quality_mod
+    from solidattention_repro_b200 import workloads
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -361,25 +630,22 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    total = args.steps + args.warmup
-    e2e_steps = min(args.steps, 500)
-    dist_steps = min(args.steps, 100)  # per-step distribution pass (after the timed region)
-    heads_mode = args.config == "cfg5" and world > 1
-    if heads_mode:
-        # KV-head sharding of one long sequence
-        from solidattention_repro_b200 import sharding
-        kv_slice = sharding.shard_kv_heads(w.kv_heads, world, rank)
-        seq_offset = 0
-    else:
-        kv_slice = None
-        seq_offset = rank * w.seqs  # sequence sharding by global batch index
+    K, W = args.steps, args.warmup
+    total = K + W
+    e2e_steps = min(K, 500)
+    dist_steps = min(K, 100)  # per-step distribution pass (after the timed region)
+    shard, kv_slice, seq_offset = job_layout(args, w, world, rank)
+    heads_mode = shard == "heads"
+    t0 = workloads.tail_for_seal_at_end(K, W)
+    seals = workloads.seal_steps(t0, W, K)
     # table room for every append of the run: warmup + timed + e2e steps. The
     # context's stream is its own (a graph cannot record the default stream).
     with torch.cuda.stream(torch.cuda.Stream(dev)):
-        ctx, info = workloads.make_context(w, total + e2e_steps + dist_steps + 64, dev, seed=1,
-                                           kv_heads_slice=kv_slice, seq_offset=seq_offset)
+        ctx, info = workloads.make_context(w, total + e2e_steps + dist_steps + 64, dev, seed=SEED,
+                                           kv_heads_slice=kv_slice, seq_offset=seq_offset,
+                                           initial_tail=t0)
     phase_bits = {}
-    queries, kv_new = workloads.decode_inputs(w, info, total, dev, seed=1 + seq_offset,
+    queries, kv_new = workloads.decode_inputs(w, info, total, dev, seed=SEED + seq_offset,
                                               kv_heads_slice=kv_slice)
     out = ctx.new_output()
     stream = ctx.stream
@@ -401,49 +667,26 @@ def main():
             dist.all_gather_into_tensor(gathered, out)
 
     with torch.cuda.stream(stream):
-        for s in range(args.warmup):
+        for s in range(W):
             step(s)
     ctx.sync()
     # NCCL's all-gather stays outside graphs; the peer-memory gather records
     use_graph = args.launch == "graph" and (not heads_mode or p2p)
-    if use_graph:
-        # record the K timed steps (nothing runs); the timed region replays them
-        with torch.cuda.stream(stream), ctx.record():
-            for s in range(args.warmup, total):
-                step(s)
-    barrier()
-    torch.cuda.synchronize()
-    launches0 = ctx.launches
-    clocks = ClockSampler(local_rank)
-    clocks.wait_first()  # the sampler is running before the region starts
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        start.record(stream)
-        if use_graph:
-            ctx.graph_launch()
-        else:
-            for s in range(args.warmup, total):
-                step(s)
-        end.record(stream)
-    end.synchronize()
-    clock_info = clocks.stop()
-    ms_local = start.elapsed_time(end)
-    gpu_launches = ctx.launches - launches0
+    ms_local, gpu_launches, clock_info = timed_steps(ctx, step, W, K, use_graph, stream, barrier)
     phase_bits["timed"] = ctx.status_bits()
     ctx.sync()
     barrier()
     torch.cuda.synchronize()
     ms = max_over_ranks(ms_local)
-    seqs_total = w.seqs if heads_mode else world * w.seqs
-    steps_per_s = seqs_total * args.steps / (ms / 1000.0)
+    seqs_total = w.seqs * (world if shard == "seqs" else 1)
+    steps_per_s = seqs_total * K / (ms / 1000.0)
 
     # ---- per-step distribution: one call per step, CUDA events between steps
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(dist_steps + 1)]
     with torch.cuda.stream(stream):
         evs[0].record(stream)
         for i in range(dist_steps):
-            step(args.warmup + i)
+            step(W + i)
             evs[i + 1].record(stream)
     evs[-1].synchronize()
     per_step = sorted(evs[i].elapsed_time(evs[i + 1]) for i in range(dist_steps))
@@ -454,7 +697,7 @@ def main():
     def pct(xs, q):
         return xs[min(len(xs) - 1, int(round(q * (len(xs) - 1))))] if xs else None
     step_dist = {"p10": pct(per_step, 0.1), "p50": pct(per_step, 0.5), "p90": pct(per_step, 0.9),
-                 "steps": dist_steps, "unit": "ms",
+                 "max": per_step[-1] if per_step else None, "steps": dist_steps, "unit": "ms",
                  "timing": "CUDA events between consecutive single-step calls, rank 0"}
 
     # ---- per-kernel roofline: each kernel alone, on its launch stream
@@ -468,8 +711,9 @@ def main():
     rep_bytes = int(sum(int(n) for n in nb_now) * ctx.qh * 128 * 4)
 
     def time_kernel(fn):
-        for _ in range(3):
-            fn()
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                fn()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
@@ -481,6 +725,13 @@ def main():
         return e0.elapsed_time(e1) / args.kernel_iters
 
     t_attn = max_over_ranks(time_kernel(lambda: ctx.attend(q_last, out)))
+    if p2p:
+        # the attention alone kept storing into every rank's gathered slot
+        # and counting arrivals: start the gather afresh on every rank
+        ctx.sync()
+        barrier()
+        ctx.gather_restart()
+        barrier()
     t_sel = max_over_ranks(time_kernel(lambda: ctx.select(q_last)))
     phase_bits["kernels"] = ctx.status_bits()
     ctx.sync()
@@ -501,8 +752,8 @@ def main():
     q_host.copy_(queries[0].reshape(-1).cpu())
     kv_host.copy_(kv_new[0].reshape(-1).cpu())
     if heads_mode:
-        # H2D of this rank's query/K/V shard, the device step, the all-gather
-        # of the per-head outputs, D2H of the assembled output
+        # H2D of this rank's query/K/V shard, the device step, the gather of
+        # the per-head outputs, D2H of the assembled output
         q_dev = torch.empty_like(queries[0])
         kv_dev = torch.empty_like(kv_new[0])
         out_host = torch.empty(tuple(gathered.shape), dtype=gathered.dtype, pin_memory=True)
@@ -528,7 +779,7 @@ def main():
         phase_bits["e2e_warmup"] = ctx.status_bits()
     barrier()
     torch.cuda.synchronize()
-    t0 = time.perf_counter()
+    t_e2e = time.perf_counter()
     e2e_times = []
     try:
         for _ in range(e2e_steps):
@@ -539,7 +790,7 @@ def main():
         phase_bits["e2e"] = ctx.status_bits()
         if any(phase_bits.values()):
             print(json.dumps({"rank": rank, "device_status_bits": phase_bits}), file=sys.stderr)
-    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    e2e_s = max_over_ranks(time.perf_counter() - t_e2e)
     e2e = {"value": seqs_total * e2e_steps / e2e_s, "unit": "steps/s",
            "h2d_bytes_per_step": q_host.numel() * 4 + kv_host.numel() * 2,
            "d2h_bytes_per_step": out_host.numel() * out_host.element_size() + 4,
@@ -549,7 +800,6 @@ def main():
                       "p90": pct(e2e_times, 0.9), "rank": 0}
 
     # ---- selection quality of the last step (dense audit, not timed)
-    from solidattention_repro_b200 import quality as quality_mod
     ctx.select(q_last)
     mass = ctx.audit(q_last)
     ctx.sync()
@@ -577,32 +827,25 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = run_cpu_baseline(ctx, w, q_last, w.layers, args.cpu_seconds, os.cpu_count() or 1)
+        cpu = run_cpu_baseline(ctx, w, q_last, args.cpu_seconds, os.cpu_count() or 1)
     ref_shapes = reference_shapes(pkg, dev) if rank == 0 and world == 1 else None
+    ctx.close()
+    replicas = None
+    if heads_mode and not args.no_replicas:
+        barrier()
+        replicas = replica_run(args, w, dev, rank, world, barrier, max_over_ranks)
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": steps_per_s, "unit": "steps/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "strong" if heads_mode else "weak",
+            "steps": K, "warmup": W, "ms_per_step": ms / K,
+            "higher_is_better": True, "scaling": "weak" if shard == "seqs" else "strong",
             "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: seeded FP16 N(0,1) KV with planted hot blocks, seeded queries",
-            "config": {
-                "workload": w.name, "layers": w.layers, "query_heads": w.query_heads,
-                "kv_heads": w.kv_heads, "head_dim": 128, "context_tokens": w.context_blocks * 32,
-                "budget_blocks": w.budget_blocks, "init_blocks": w.init_blocks,
-                "local_blocks": w.local_blocks, "seqs_per_gpu": w.seqs,
-                "context_min_tokens": (w.context_min_blocks or w.context_blocks) * 32,
-                "parallelism": (f"kv-head-sharded x{world}, outputs gathered by "
-                                + ("the attention kernel's peer-memory stores (NVLink P2P)"
-                                   if p2p else "an NCCL all-gather") + " every step"
-                                if heads_mode else
-                                f"sequence-sharded x{world}" if world > 1 else "single"),
-                "l2": "inputs larger than L2: each step reads its selected KV and all "
-                      "representatives (>1 GB at cfg3)",
-                "kv_dtype": "fp16", "accumulate": "fp32",
-                "launch": ("one CUDA graph of the timed steps (sa_ctx_graph_launch)" if use_graph
-                           else "one sa_ctx_step call per step")},
+            "config": job_config(args, w, world, shard, t0),
+            "launch": ("one CUDA graph of the timed steps (sa_ctx_graph_launch)" if use_graph
+                       else "one sa_ctx_step call per step"),
+            "seals_in_timed_region": seals,
             "step_ms_distribution": step_dist,
             "selected_kv_gbs": attn_gbs, "selected_kv_frac": attn_gbs / hbm,
             # selected KV (16-token average tail) per GPU-step x per-GPU steps/s
@@ -615,18 +858,43 @@ def main():
                 "attention": {"ms": t_attn, "bytes": kv_bytes, "gbs": attn_gbs,
                               "frac": attn_gbs / hbm},
                 "select": {"ms": t_sel, "bytes": rep_bytes, "gbs": sel_gbs,
-                           "frac": sel_gbs / hbm}},
+                           "frac": sel_gbs / hbm},
+                "rest_of_step_ms": ms / K - t_attn - t_sel,
+                "timing": "each kernel alone, CUDA events over back-to-back launches, max over "
+                          "ranks; rest_of_step_ms = the step minus both (seal, gather, launch "
+                          "gaps, and the overlap that chaining them gains)"},
             "quality": qual,
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": gpu_launches,
+            "replicas": replicas,
             "reference_shapes": ref_shapes,
             "device_status_bits": phase_bits,
             "clocks": clock_info,
         }
         print(json.dumps(line), flush=True)
-    ctx.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    import __graft_entry__
+
+    pkg = __graft_entry__.load_package()
+    from solidattention_repro_b200 import workloads
+
+    w = workloads.CONFIGS[args.config]
+    if args.layers:
+        import dataclasses
+        w = dataclasses.replace(w, layers=args.layers, name=f"{w.name}-{args.layers}layers")
+    if args.impl == "reference":
+        reference_arm(args, w, rank, world)
+        return
+    our_arm(args, w, rank, world, local_rank, pkg)
 
 
 if __name__ == "__main__":

@@ -102,10 +102,14 @@ SA_API sa_status sa_attention_packed(const uint16_t* kv, const float* query,
  * It allocates nothing: its split-K scratch is a 2 MiB static device array,
  * held by every GPU that loads this library until the process exits.
  * Problems whose workspace (sa_attention_workspace_size) exceeds 2 MiB are
- * refused with SA_ERR_CAPACITY. The first call on a device looks up the
- * array's device address (cudaGetSymbolAddress); make that first call before
- * any stream capture. All calls share the one array, so calls that overlap on
- * the GPU (other streams, other host threads) race; serialise them.
+ * refused with SA_ERR_CAPACITY. Every call made outside a stream capture
+ * looks up the array's device address on the current device
+ * (cudaGetSymbolAddress), so the address follows a device reset; a call
+ * made while its stream is capturing reuses the address of the last such
+ * call on that device, so make a first call on each device before any
+ * stream capture (a capture with none before it is refused). All calls
+ * share the one array, so calls that overlap on the GPU (other streams,
+ * other host threads) race; serialise them.
  * This entry point has no counterpart in the reference. */
 SA_API sa_status sa_attention_packed_noalloc(const uint16_t* kv,
                                              const float* query, size_t tokens,
@@ -404,14 +408,23 @@ SA_API sa_status sa_ctx_export_blocks(sa_ctx* ctx, int32_t seq, int32_t layer, i
 /* Allocate (once) this rank's gathered buffer for `world` ranks. */
 SA_API sa_status sa_ctx_gather_buffer(sa_ctx* ctx, int32_t world, void** buf_out,
                                       size_t* bytes_out);
-/* peer_bufs: host array [world] of device pointers, peer_bufs[rank] = own. */
+/* peer_bufs: host array [world] of device pointers, peer_bufs[rank] = own.
+ * Attaching (again) synchronizes the context stream and zeroes this rank's
+ * arrival counter and epoch. After a wait timed out (SA_ERR_TIMEOUT), late
+ * arrivals of that step could satisfy a later wait early, so every rank
+ * re-attaches, with no gathered step in flight anywhere, before the next
+ * gathered step. */
 SA_API sa_status sa_ctx_gather_attach(sa_ctx* ctx, int32_t rank, void* const* peer_bufs);
 /* Enqueue the wait for the latest attention's outputs from every rank;
  * *gathered_out (nullable) = the slot holding them [seqs][layers][world*QH][D].
  * A wait that gives up sets SA_DEV_TIMEOUT in the status word. The slot
  * parity and the expected arrival count are kept on the device, so
  * attention + wait pairs recorded with sa_ctx_graph_begin replay correctly
- * (every attention must be followed by its wait before the next one). */
+ * (every attention must be followed by its wait before the next one). A
+ * slot address handed out while recording stays fixed in the graph while
+ * every replay advances the parity once per gathered attention, so
+ * sa_ctx_graph_end refuses (SA_ERR_UNSUPPORTED) a recording that handed one
+ * out and holds an odd number of gathered attentions. */
 SA_API sa_status sa_ctx_gather_wait(sa_ctx* ctx, void** gathered_out);
 /* CUDA IPC handle of a device allocation (SA_IPC_HANDLE_BYTES bytes), and
  * mapping / unmapping another process's allocation on `device`. */

@@ -31,21 +31,35 @@ _i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
 _sz = C.c_size_t
 
 
-# Where the reference project is checked out in the build container; the
-# environment variable SA_REFERENCE_ROOT overrides it. The GPU box has none.
-DEFAULT_REFERENCE_ROOT = "/root/reference"
-
-
-def reference_root_dir(reference_root: str | None = None) -> str:
-    return reference_root or os.environ.get("SA_REFERENCE_ROOT", DEFAULT_REFERENCE_ROOT)
+def reference_root_dir(reference_root: str | None = None) -> str | None:
+    """The reference project's checkout: the caller's path, else the
+    SA_REFERENCE_ROOT environment variable, else a checkout named `reference`
+    beside this repository's directory; None when none of them holds the
+    reference's sources (a machine that only runs the prebuilt libraries)."""
+    candidates = [reference_root, os.environ.get("SA_REFERENCE_ROOT"),
+                  str(HERE.parent.parent / "reference")]
+    for c in candidates:
+        if c and Path(c, "cpp", "src", "selection.cpp").exists():
+            return c
+    return None
 
 
 def build(reference_root: str | None = None) -> None:
     """Compile liboracle.so, and _ref/libsa_ref.so when the reference tree exists."""
     subprocess.run(["make", "-s", "-C", str(HERE), "all"], check=True)
     ref = reference_root_dir(reference_root)
-    if Path(ref, "cpp", "src", "selection.cpp").exists():
+    if ref is not None:
         subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={ref}"], check=True)
+
+
+class Unit(C.Structure):
+    """One (sequence, layer, KV head) of a CPU decode step (sao_unit /
+    saref_unit): blocks [nb + 1][32][2][KH][D] FP16 (sealed blocks, then the
+    open tail), reps [QH][nb][D] FP32, query [QH][D] FP32, ids_out [budget]
+    int64, out [QH/KH][D] FP32."""
+    _fields_ = [("blocks", C.c_void_p), ("reps", C.c_void_p), ("query", C.c_void_p),
+                ("nb", _sz), ("tail_len", _sz), ("kv_head", _sz), ("ids_out", C.c_void_p),
+                ("out", C.c_void_p)]
 
 
 class _Lib:
@@ -61,6 +75,10 @@ class _Lib:
         getattr(L, f"{p}attention").argtypes = [_u16p, _f32p, _sz, _sz, _sz, _sz, C.c_float, _f32p]
         getattr(L, f"{p}select_shared_blocks").argtypes = [
             _f32p, _f32p, _sz, _sz, _sz, _sz, _sz, _sz, _i64p, C.POINTER(_sz), C.c_void_p]
+        getattr(L, f"{p}sparse_units").argtypes = [
+            C.POINTER(Unit), _sz, _sz, _sz, _sz, _sz, _sz, _sz, _sz, C.c_float, C.c_int]
+        getattr(L, f"{p}build_reps_per_block").argtypes = [
+            _f32p, _u16p, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _f32p, C.c_int]
         getattr(L, f"{p}sparse_step").argtypes = [
             _u16p, _i32p, _sz, _f32p, _f32p, _i32p, _sz, _sz, _sz, _sz, _sz, _sz, _sz,
             _sz, _sz, _sz, C.c_float, C.c_int, _i64p, _f32p]
@@ -122,6 +140,27 @@ class _Lib:
             raise ValueError("invalid local-causal representative dimensions")
         return (values[: qh * blocks * d].reshape(qh, blocks, d),
                 offsets[: qh * blocks * topk].reshape(qh, blocks, topk))
+
+    def sparse_units(self, units, qh, kh, d, budget, init, local, scale, threads):
+        """Run a ctypes array of Unit (arrays it points to kept alive by the
+        caller): per unit select over its KV head's group, packed gather,
+        attention; `threads` OpenMP threads over the units."""
+        rc = getattr(self.lib, f"{self.prefix}sparse_units")(
+            units, len(units), qh, kh, d, 32, budget, init, local, float(scale), int(threads))
+        if rc != 0:
+            raise ValueError("sparse units step failed")
+
+    def build_reps_per_block(self, prompt_q, kv, blocks, qh, kh, d, window, topk, threads):
+        """Representatives [QH][blocks][D] of consecutive 32-token blocks, each
+        block built alone (the online seal's call); OpenMP over blocks."""
+        values = np.zeros((qh, blocks, d), np.float32)
+        rc = getattr(self.lib, f"{self.prefix}build_reps_per_block")(
+            np.ascontiguousarray(prompt_q, np.float32).reshape(-1),
+            np.ascontiguousarray(kv, np.uint16).reshape(-1), blocks, qh, kh, d, 32, window, topk,
+            values.reshape(-1), int(threads))
+        if rc != 0:
+            raise ValueError("invalid representative dimensions")
+        return values
 
     def sparse_step(self, pool, table, reps, query, tail_block, tail_len, qh, kh, d,
                     block_tokens, blocks, budget, init, local, scale, threads):

@@ -153,6 +153,106 @@ int saref_sparse_step(const std::uint16_t* pool, const std::int32_t* table,
   return failed ? -1 : 0;
 }
 
+// The per-unit body of saref_sparse_step over a caller's list of units, so
+// that units of sequence-layers with different block counts share one
+// parallel loop. Unit layout as sao_unit (oracle/sa_oracle.h): the unit's
+// sealed blocks in logical order followed by its open tail block.
+struct saref_unit {
+  const std::uint16_t* blocks;
+  const float* reps;
+  const float* query;
+  std::size_t nb;
+  std::size_t tail_len;
+  std::size_t kv_head;
+  std::int64_t* ids_out;
+  float* out;
+};
+
+int saref_sparse_units(const saref_unit* units, std::size_t n, std::size_t query_heads,
+                       std::size_t kv_heads, std::size_t head_dim, std::size_t block_tokens,
+                       std::size_t budget, std::size_t init, std::size_t local, float scale,
+                       int threads) {
+  if (kv_heads == 0 || query_heads % kv_heads != 0) return -1;
+  const std::size_t group = query_heads / kv_heads;
+  const std::size_t token_values = 2 * kv_heads * head_dim;
+  int failed = 0;
+#ifdef _OPENMP
+#pragma omp parallel for num_threads(threads) schedule(dynamic, 1) reduction(| : failed)
+#endif
+  for (long i = 0; i < static_cast<long>(n); ++i) {
+    const saref_unit& u = units[i];
+    const std::size_t h = u.kv_head;
+    try {
+      const float* q = u.query + h * group * head_dim;
+      const float* r = u.reps + h * group * u.nb * head_dim;
+      const std::size_t eff = budget < u.nb ? budget : u.nb;
+      const std::size_t ini = init < eff ? init : eff;
+      const std::size_t loc = local < eff - ini ? local : eff - ini;
+      const auto sel = sa::select_shared_blocks(q, r, group, u.nb, head_dim, eff, ini, loc);
+      const std::size_t tokens = sel.block_ids.size() * block_tokens + u.tail_len;
+      std::vector<std::uint16_t> packed(tokens * 2 * head_dim);
+      std::size_t row = 0;
+      auto copy_rows = [&](std::size_t block, std::size_t rows) {
+        for (std::size_t t = 0; t < rows; ++t, ++row) {
+          const std::uint16_t* src = u.blocks + (block * block_tokens + t) * token_values;
+          std::memcpy(&packed[row * 2 * head_dim], src + h * head_dim,
+                      head_dim * sizeof(std::uint16_t));
+          std::memcpy(&packed[row * 2 * head_dim + head_dim],
+                      src + kv_heads * head_dim + h * head_dim, head_dim * sizeof(std::uint16_t));
+        }
+      };
+      for (std::size_t k = 0; k < sel.block_ids.size(); ++k) {
+        u.ids_out[k] = static_cast<std::int64_t>(sel.block_ids[k]);
+        copy_rows(sel.block_ids[k], block_tokens);
+      }
+      copy_rows(u.nb, u.tail_len);
+      sa::AttentionProblem p{packed.data(), q, tokens, group, 1, head_dim, scale};
+      const auto o = sa::attention_reference(p);
+      std::memcpy(u.out, o.data(), o.size() * sizeof(float));
+    } catch (const std::exception&) {
+      failed |= 1;
+    }
+  }
+  return failed ? -1 : 0;
+}
+
+// Representatives of consecutive blocks, each block its own call of the
+// reference's build_local_causal_representatives (T = block_tokens), as the
+// online seal builds them (cpp/src/online_seal_main.cpp:41). prompt_queries
+// [query_heads][blocks * block_tokens][head_dim]; kv token rows; values_out
+// [query_heads][blocks][head_dim]; OpenMP over blocks.
+int saref_build_reps_per_block(const float* prompt_queries, const std::uint16_t* kv,
+                               std::size_t blocks, std::size_t query_heads,
+                               std::size_t kv_heads, std::size_t head_dim,
+                               std::size_t block_tokens, std::size_t local_window,
+                               std::size_t topk, float* values_out, int threads) {
+  const std::size_t tokens = blocks * block_tokens;
+  const std::size_t token_values = 2 * kv_heads * head_dim;
+  int failed = 0;
+#ifdef _OPENMP
+#pragma omp parallel for num_threads(threads) schedule(dynamic, 4) reduction(| : failed)
+#endif
+  for (long b = 0; b < static_cast<long>(blocks); ++b) {
+    try {
+      std::vector<float> pq(query_heads * block_tokens * head_dim);
+      for (std::size_t h = 0; h < query_heads; ++h)
+        std::memcpy(&pq[h * block_tokens * head_dim],
+                    prompt_queries + (h * tokens + static_cast<std::size_t>(b) * block_tokens) *
+                                         head_dim,
+                    block_tokens * head_dim * sizeof(float));
+      const auto r = sa::build_local_causal_representatives(
+          pq.data(), kv + static_cast<std::size_t>(b) * block_tokens * token_values,
+          block_tokens, query_heads, kv_heads, head_dim, block_tokens, local_window, topk);
+      for (std::size_t h = 0; h < query_heads; ++h)
+        std::memcpy(values_out + (h * blocks + static_cast<std::size_t>(b)) * head_dim,
+                    r.values.data() + h * head_dim, head_dim * sizeof(float));
+    } catch (const std::exception&) {
+      failed |= 1;
+    }
+  }
+  return failed ? -1 : 0;
+}
+
 int saref_max_threads() {
 #ifdef _OPENMP
   return omp_get_max_threads();

@@ -511,6 +511,87 @@ int sao_sparse_step(const uint16_t* pool, const int32_t* table,
   return failed ? -1 : 0;
 }
 
+/* The unit body of sao_sparse_step (select per KV-head group, packed gather
+ * of the chosen blocks and the tail in ascending order as
+ * selection_main.cpp:196-218 packs them, attention) over a caller's list. */
+int sao_sparse_units(const sao_unit* units, size_t n, size_t query_heads, size_t kv_heads,
+                     size_t head_dim, size_t block_tokens, size_t budget, size_t init,
+                     size_t local, float scale, int threads) {
+  if (kv_heads == 0 || query_heads % kv_heads != 0) return -1;
+  const size_t group = query_heads / kv_heads;
+  const size_t token_values = 2 * kv_heads * head_dim;
+  int failed = 0;
+#ifdef _OPENMP
+#pragma omp parallel for num_threads(threads) schedule(dynamic, 1) reduction(| : failed)
+#endif
+  for (long i = 0; i < (long)n; ++i) {
+    const sao_unit* u = &units[i];
+    const size_t h = u->kv_head;
+    const float* q = u->query + h * group * head_dim;
+    const float* r = u->reps + h * group * u->nb * head_dim;
+    const size_t eff = budget < u->nb ? budget : u->nb;
+    const size_t ini = init < eff ? init : eff;
+    const size_t loc = local < eff - ini ? local : eff - ini;
+    size_t count = 0;
+    if (sao_select_shared_blocks(q, r, group, u->nb, head_dim, eff, ini, loc, u->ids_out,
+                                 &count, NULL) != 0) {
+      failed |= 1;
+      continue;
+    }
+    const size_t tokens = count * block_tokens + u->tail_len;
+    uint16_t* packed = (uint16_t*)malloc((tokens ? tokens : 1) * 2 * head_dim * sizeof(uint16_t));
+    size_t row = 0;
+    for (size_t k = 0; k <= count; ++k) {
+      const size_t block = k < count ? (size_t)u->ids_out[k] : u->nb;
+      const size_t rows = k < count ? block_tokens : u->tail_len;
+      for (size_t t = 0; t < rows; ++t, ++row) {
+        const uint16_t* src = u->blocks + (block * block_tokens + t) * token_values;
+        memcpy(packed + row * 2 * head_dim, src + h * head_dim, head_dim * sizeof(uint16_t));
+        memcpy(packed + row * 2 * head_dim + head_dim, src + kv_heads * head_dim + h * head_dim,
+               head_dim * sizeof(uint16_t));
+      }
+    }
+    if (tokens == 0 || sao_attention(packed, q, tokens, group, 1, head_dim, scale, u->out) != 0)
+      failed |= 1;
+    free(packed);
+  }
+  return failed ? -1 : 0;
+}
+
+int sao_build_reps_per_block(const float* prompt_queries, const uint16_t* kv, size_t blocks,
+                             size_t query_heads, size_t kv_heads, size_t head_dim,
+                             size_t block_tokens, size_t local_window, size_t topk,
+                             float* values_out, int threads) {
+  if (blocks == 0 || block_tokens == 0 || topk == 0) return -1;
+  const size_t tokens = blocks * block_tokens;
+  const size_t token_values = 2 * kv_heads * head_dim;
+  int failed = 0;
+#ifdef _OPENMP
+#pragma omp parallel for num_threads(threads) schedule(dynamic, 4) reduction(| : failed)
+#endif
+  for (long b = 0; b < (long)blocks; ++b) {
+    float* pq = (float*)malloc(query_heads * block_tokens * head_dim * sizeof(float));
+    float* values = (float*)malloc(query_heads * head_dim * sizeof(float));
+    int64_t* offsets = (int64_t*)malloc(query_heads * topk * sizeof(int64_t));
+    for (size_t h = 0; h < query_heads; ++h)
+      memcpy(pq + h * block_tokens * head_dim,
+             prompt_queries + (h * tokens + (size_t)b * block_tokens) * head_dim,
+             block_tokens * head_dim * sizeof(float));
+    if (sao_build_representatives(pq, kv + (size_t)b * block_tokens * token_values, block_tokens,
+                                  query_heads, kv_heads, head_dim, block_tokens, local_window,
+                                  topk, values, offsets, NULL) != 0)
+      failed |= 1;
+    else
+      for (size_t h = 0; h < query_heads; ++h)
+        memcpy(values_out + (h * blocks + (size_t)b) * head_dim, values + h * head_dim,
+               head_dim * sizeof(float));
+    free(offsets);
+    free(values);
+    free(pq);
+  }
+  return failed ? -1 : 0;
+}
+
 /* kv_lifecycle_main.cpp:93-103: the four highest-scoring in-block offsets,
  * each pass taking the first strict maximum among offsets not yet taken. */
 void sao_top4_first_max(const float* scores, size_t block_tokens, int64_t* out) {

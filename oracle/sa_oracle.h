@@ -134,6 +134,40 @@ int sao_sparse_step(const uint16_t* pool, const int32_t* table,
                     size_t init, size_t local, float scale, int threads,
                     int64_t* ids_out, float* out);
 
+/* One decode work unit of the CPU path: a (sequence, layer, KV head).
+ * blocks: [nb + 1][block_tokens][2][kv_heads][head_dim] FP16, the nb sealed
+ * blocks in logical order followed by the open tail block (tail_len rows
+ * valid); reps: [query_heads][nb][head_dim]; query: [query_heads][head_dim]
+ * (every head of the sequence-layer; the unit uses its KV head's group);
+ * ids_out: [budget]; out: [query_heads / kv_heads][head_dim]. */
+typedef struct {
+  const uint16_t* blocks;
+  const float* reps;
+  const float* query;
+  size_t nb;
+  size_t tail_len;
+  size_t kv_head;
+  int64_t* ids_out;
+  float* out;
+} sao_unit;
+
+/* The per-unit body of sao_sparse_step over a list of units, `threads`
+ * OpenMP threads over the units. */
+int sao_sparse_units(const sao_unit* units, size_t n, size_t query_heads, size_t kv_heads,
+                     size_t head_dim, size_t block_tokens, size_t budget, size_t init,
+                     size_t local, float scale, int threads);
+
+/* Representatives of `blocks` consecutive blocks, each built alone as the
+ * online seal does (cpp/src/online_seal_main.cpp:41: one call of
+ * build_local_causal_representatives per block, T = block_tokens):
+ * prompt_queries [query_heads][blocks * block_tokens][head_dim], kv token
+ * rows [blocks * block_tokens][2][kv_heads][head_dim] FP16, values_out
+ * [query_heads][blocks][head_dim]; `threads` OpenMP threads over blocks. */
+int sao_build_reps_per_block(const float* prompt_queries, const uint16_t* kv, size_t blocks,
+                             size_t query_heads, size_t kv_heads, size_t head_dim,
+                             size_t block_tokens, size_t local_window, size_t topk,
+                             float* values_out, int threads);
+
 /* The lifecycle's representative audit (kv_lifecycle_main.cpp:93-103): four
  * in-block offsets by descending score, first maximum wins. */
 void sao_top4_first_max(const float* scores, size_t block_tokens, int64_t* out);

@@ -504,15 +504,25 @@ class DecodeContext:
             self._opened.append(int(ptr.value))
             ptrs.append(int(ptr.value))
         self.gather_attach(rank, ptrs)
+        self._gather_ptrs = (rank, ptrs)
+
+    def gather_restart(self) -> None:
+        """Re-attach the buffers of enable_gather: zero this rank's arrival
+        counter and epoch (every rank calls it, with no gathered attention in
+        flight anywhere, e.g. after attention launches without their waits or
+        after a timed-out wait)."""
+        rank, ptrs = self._gather_ptrs
+        self.gather_attach(rank, ptrs)
 
     def gather_wait(self, view: bool = True) -> torch.Tensor | None:
         """Enqueue the wait for every rank's outputs of the latest attention;
         returns the gathered slot [S, L, world*QH, 128] (valid until the
         attention after next), or None when view is False."""
+        if not view:
+            check(self._lib.sa_ctx_gather_wait(self._h, None), "sa_ctx_gather_wait")
+            return None
         ptr = C.c_void_p()
         check(self._lib.sa_ctx_gather_wait(self._h, C.byref(ptr)), "sa_ctx_gather_wait")
-        if not view:
-            return None
         return _view(int(ptr.value), (self.seqs, self.layers, self._gather_world * self.qh, HEAD_DIM),
                      torch.float16 if self.out_fp16 else torch.float32, self.device)
 

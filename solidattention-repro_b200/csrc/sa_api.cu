@@ -53,6 +53,25 @@ class DeviceGuard {
 
 }  // namespace
 
+int device_sm_count() {
+  static int cached[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return 148;
+  }
+  if (cached[dev] <= 0) {
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        sms <= 0) {
+      cudaGetLastError();
+      return 148;
+    }
+    cached[dev] = sms;
+  }
+  return cached[dev];
+}
+
 sa_status ensure_smem_limit(const void* kernel, int bytes, int* configured_per_device) {
   int dev = 0;
   SA_CUDA_TRY(cudaGetDevice(&dev));
@@ -123,6 +142,7 @@ struct sa_ctx {
   bool recording = false;
   uint64_t launches_before_recording = 0;
   uint64_t gather_attends_before_recording = 0;
+  bool gather_view_recorded = false;  // a gathered-slot view was handed out while recording
   uint64_t graph_launches = 0;        // kernel launches one replay issues
   uint64_t graph_gather_attends = 0;  // gathered attends one replay issues
   cudaGraph_t graph = nullptr;
@@ -161,10 +181,11 @@ SA_API const char* sa_version(void) { return "sa_b200 0.1 sm_100a"; }
 
 SA_API size_t sa_attention_workspace_size(size_t tokens, size_t query_heads, size_t kv_heads) {
   if (kv_heads == 0 || query_heads % kv_heads != 0) return 0;
+  if (tokens > 0xffffffffull) return 0;  // beyond what sa_attention_packed accepts
   const int entries = (int)((tokens + kBlockTokens - 1) / kBlockTokens);
   const int units = (int)kv_heads;
   const int group = (int)(query_heads / kv_heads);
-  const AttnPlan plan = attention_plan(units, std::max(entries, 1), group);
+  const AttnPlan plan = attention_plan(units, std::max(entries, 1), group, device_sm_count());
   return attention_scratch_bytes(plan, units, group) + (size_t)units * sizeof(int) + 256;
 }
 
@@ -210,7 +231,7 @@ SA_API sa_status sa_attention_packed(const uint16_t* kv, const float* query, siz
   p.out = out;
   p.out_fp16 = out_fp16;
   p.scale_log2 = scale * 1.4426950408889634f;
-  const AttnPlan plan = attention_plan(units, entries, p.group);
+  const AttnPlan plan = attention_plan(units, entries, p.group, device_sm_count());
   p.slots_per_unit = plan.slots_per_unit;
   p.max_segments = plan.max_segments;
   p.ctas = plan.ctas;
@@ -738,7 +759,7 @@ SA_API sa_status sa_ctx_create(const sa_ctx_config* config, sa_ctx** out) {
   d.rep_topk = g.rep_topk;
   d.rep_scale = 1.0f / std::sqrt((float)kHeadDim);
   const int units = c->num_sl * g.kv_heads;
-  c->attn_plan = attention_plan(units, g.budget_blocks + 1, c->group);
+  c->attn_plan = attention_plan(units, g.budget_blocks + 1, c->group, device_sm_count());
 
   st = cuda_status(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "cudaStreamCreate");
   c->own_stream = st == SA_OK;
@@ -1088,6 +1109,7 @@ SA_API sa_status sa_ctx_graph_begin(sa_ctx* c) {
   c->recording = true;
   c->launches_before_recording = c->launches;
   c->gather_attends_before_recording = c->gather_attends;
+  c->gather_view_recorded = false;
   return SA_OK;
 }
 
@@ -1103,6 +1125,16 @@ SA_API sa_status sa_ctx_graph_end(sa_ctx* c) {
   c->gather_attends = c->gather_attends_before_recording;
   cudaGraph_t graph = nullptr;
   SA_CUDA_TRY(cudaStreamEndCapture(c->stream, &graph));
+  if (c->gather_view_recorded && recorded_attends % 2 == 1) {
+    // Every replay flips the device-side slot parity once per gathered
+    // attention, while a recorded consumer keeps the slot address it was
+    // given at record time: with an odd count it would read the previous
+    // step's slot on every second replay.
+    cudaGraphDestroy(graph);
+    return fail(SA_ERR_UNSUPPORTED,
+                "graph_end: a recording that hands out a gathered slot must hold an even "
+                "number of gathered attentions");
+  }
   cudaGraphExec_t exec = nullptr;
   cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
   if (e == cudaSuccess) e = cudaGraphUpload(exec, c->stream);
@@ -1264,6 +1296,11 @@ SA_API sa_status sa_ctx_gather_attach(sa_ctx* c, int32_t rank, void* const* peer
   }
   SA_CUDA_TRY(cudaMemcpy(c->gather_peers, peer_bufs, sizeof(void*) * c->gather_world,
                          cudaMemcpyHostToDevice));
+  // A fresh start: arrival counter and epoch zero (late arrivals of a step
+  // whose wait timed out are dropped with them), slot parity even.
+  SA_CUDA_TRY(cudaStreamSynchronize(c->stream));
+  SA_CUDA_TRY(cudaMemset(c->gather_buf + c->gather_counter_bytes, 0, 16));
+  c->gather_attends = 0;
   c->gather_rank = rank;
   return SA_OK;
 }
@@ -1280,8 +1317,10 @@ SA_API sa_status sa_ctx_gather_wait(sa_ctx* c, void** gathered_out) {
       reinterpret_cast<unsigned long long*>(c->gather_buf + c->gather_counter_bytes + 8),
       c->gather_world * units, c->dev.status, c->stream);
   if (st != SA_OK) return st;
-  if (gathered_out)
+  if (gathered_out) {
     *gathered_out = c->gather_buf + ((c->gather_attends - 1) % 2) * c->gather_slot_bytes;
+    if (c->recording) c->gather_view_recorded = true;
+  }
   return SA_OK;
 }
 

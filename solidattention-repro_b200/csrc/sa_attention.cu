@@ -63,7 +63,6 @@ constexpr int kStageBytes = 2 * kEntryBytes;            // two entries per stage
 constexpr int kPartialStride = 2 + kHeadDim;            // m, l, o[128]
 constexpr int kMaxCtaSlots = 512;                       // slots one CTA may own
 constexpr int kMaxSegments = 32;                        // units one CTA may touch
-constexpr int kSms = 148;                               // B200
 constexpr unsigned kFull = 0xffffffffu;
 constexpr float kLazyRescale = 8.f;                     // log2 units
 
@@ -691,11 +690,11 @@ sa_status launch_gather_wait(const unsigned long long* counter, unsigned long lo
   return cuda_status(cudaGetLastError(), "gather_wait_kernel launch");
 }
 
-AttnPlan attention_plan(int units, int slots_per_unit, int group) {
+AttnPlan attention_plan(int units, int slots_per_unit, int group, int sms) {
   const long long E = std::max(1, slots_per_unit);
   const long long U = std::max(1, units);
   const long long total = U * E;
-  const long long wave = (long long)kSms * (group <= 4 ? 2 : 1);  // resident CTAs
+  const long long wave = (long long)std::max(1, sms) * (group <= 4 ? 2 : 1);  // resident CTAs
   // Estimated time of a CTA count, in stage times (two slots per stage): the
   // CTAs run in ceil(C / wave) waves; a segment end (the 8-warp merge and the
   // next unit's start) costs about five stages, and a unit split over n CTAs

@@ -50,6 +50,12 @@ cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_
 sa_status ensure_smem_limit(const void* kernel, int bytes, int* configured_per_device);
 constexpr int kMaxDevices = 64;
 
+// Streaming multiprocessors of the current device (cached per device; 148,
+// a whole B200, when no device can be queried, e.g. a size query on a host
+// without a GPU). Grid plans scale with it, so a context on a partitioned
+// device (an MPS or green-context share) gets a plan for the SMs it has.
+int device_sm_count();
+
 // ---- decode-context device state (owned by sa_api.cu) -------------------------
 
 struct CtxDev {
@@ -136,7 +142,7 @@ struct AttnPlan {
   int max_segments;
   int ctas;
 };
-AttnPlan attention_plan(int units, int slots_per_unit, int group);
+AttnPlan attention_plan(int units, int slots_per_unit, int group, int sms);
 size_t attention_scratch_bytes(const AttnPlan& plan, int units, int group);
 sa_status launch_attention(const AttnParams& p, cudaStream_t stream);
 // Waits (bounded, one thread) until *counter >= expected with system-scope

@@ -512,7 +512,7 @@ sa_status launch_seal(const CtxDev& c, int pending, cudaStream_t stream, bool pd
     return st;
   // three CTAs per SM at most; a step that fills no tail runs CTA 0 alone
   const int items = c.qh * c.num_sl;
-  const int grid = std::max(1, std::min(items, 3 * 148));
+  const int grid = std::max(1, std::min(items, 3 * device_sm_count()));
   return cuda_status(launch_kernel(seal_kernel, dim3(grid), dim3(kRepThreads), sizeof(RepSmem),
                                    stream, pdl, c, pending),
                      "seal_kernel launch");

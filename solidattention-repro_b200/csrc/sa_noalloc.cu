@@ -27,18 +27,28 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 void* g_scratch_address[sa::kMaxDevices];
 std::mutex g_scratch_mutex;
 
-sa_status scratch_address_for_current_device(void** out) {
+// The array's device address on the current device. Outside a stream
+// capture it is looked up on every call (cheap once the module is loaded),
+// so a device reset or a new primary context never leaves a stale address
+// behind; while `stream` is capturing, the address of the last uncaptured
+// call on this device is used, and a device that has had none is refused.
+sa_status scratch_address_for_current_device(cudaStream_t stream, void** out) {
   int device = 0;
   SA_CUDA_TRY(cudaGetDevice(&device));
   if (device < 0 || device >= sa::kMaxDevices)
     return sa::fail(SA_ERR_UNSUPPORTED, "attention_noalloc: device index above 63");
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  SA_CUDA_TRY(cudaStreamIsCapturing(stream, &capture));
   std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (!g_scratch_address[device]) {
+  if (capture == cudaStreamCaptureStatusNone) {
     void* address = nullptr;
     const cudaError_t err = cudaGetSymbolAddress(&address, g_noalloc_scratch);
     if (err != cudaSuccess)
       return sa::cuda_status(err, "cudaGetSymbolAddress(no-alloc attention scratch)");
     g_scratch_address[device] = address;
+  } else if (!g_scratch_address[device]) {
+    return sa::fail(SA_ERR_INVALID_ARG,
+                    "attention_noalloc: make a first call on this device before stream capture");
   }
   *out = g_scratch_address[device];
   return SA_OK;
@@ -61,7 +71,8 @@ extern "C" SA_API sa_status sa_attention_packed_noalloc(const uint16_t* kv, cons
                         " bytes of scratch, above the 2 MiB static array; use "
                         "sa_attention_packed with a caller workspace");
   void* scratch = nullptr;
-  const sa_status st = scratch_address_for_current_device(&scratch);
+  const sa_status st =
+      scratch_address_for_current_device(static_cast<cudaStream_t>(stream), &scratch);
   if (st != SA_OK) return st;
   // The same kernel as sa_attention_packed, with the static array as its
   // workspace; that call clears the arrival counters before launching.

@@ -40,7 +40,7 @@ constexpr int kWarpBlocks = 32 * kLaneBlocks;       // 128 blocks per warp pass
 constexpr int kMaxBlocks = 16384;
 constexpr int kDimUnroll = 8;        // dims in flight per warp: occupancy-bound grids
 constexpr int kDimUnrollDeep = 16;   // grids of at most kDeepGridCtas CTAs (latency-bound)
-constexpr int kDeepGridCtas = 5 * 148;
+constexpr int kDeepCtasPerSm = 5;   // the deep variant's resident CTAs per SM
 constexpr unsigned kFull = 0xffffffffu;
 
 constexpr int kTieMax = kThreads;  // threshold buckets this small are ranked directly
@@ -593,7 +593,8 @@ sa_status launch_select(const SelectParams& p, cudaStream_t stream) {
                topk_smem_bytes(p.nb_cap));
   const int nchunks = std::max(1, (p.nb_cap + chunk - 1) / chunk);
   const dim3 grid(nchunks, p.num_sl * p.n_groups, hsplit);
-  const bool deep = (long long)nchunks * p.num_sl * p.n_groups * hsplit <= kDeepGridCtas;
+  const bool deep =
+      (long long)nchunks * p.num_sl * p.n_groups * hsplit <= (long long)kDeepCtasPerSm * device_sm_count();
   auto kernel = deep ? select_kernel<kDimUnrollDeep, 5> : select_kernel<kDimUnroll, 10>;
   static int configured[2][kMaxDevices];
   const sa_status st = ensure_smem_limit((const void*)kernel, (int)std::max<size_t>(smem, 48 * 1024),

@@ -1,7 +1,8 @@
 """Generate the golden vectors under tests/golden/ from the reference itself.
 
 Run in a container that has the reference tree (its root given by --reference,
-else SA_REFERENCE_ROOT, else oracle.DEFAULT_REFERENCE_ROOT) and the compiled
+else SA_REFERENCE_ROOT, else a checkout named `reference` beside this
+repository) and the compiled
 reference (oracle/_ref, built by `python __graft_entry__.py build`):
 
     python tests/golden/make_golden.py [--reference <reference root>]
@@ -107,12 +108,15 @@ def main():
     sys.path.insert(0, str(HERE))
     import oracle
 
-    oracle.build(oracle.reference_root_dir(args.reference))
+    root = oracle.reference_root_dir(args.reference)
+    if root is None:
+        raise SystemExit("the reference tree was not found (--reference or SA_REFERENCE_ROOT)")
+    oracle.build(root)
     ref = oracle.reference()
     if ref is None:
         raise SystemExit("oracle/_ref was not built: the reference tree is required")
     np.savez_compressed(HERE / "golden_ref.npz", **make_ref_vectors(ref))
-    (HERE / "python_twins.json").write_text(json.dumps(make_python_twins(Path(args.reference))))
+    (HERE / "python_twins.json").write_text(json.dumps(make_python_twins(Path(root))))
     print("wrote", HERE / "golden_ref.npz", HERE / "python_twins.json")
 
 

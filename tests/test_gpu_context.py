@@ -342,6 +342,55 @@ def test_recorded_gather_steps_replay_like_eager_steps(pkg, cuda):
         c.close()
 
 
+def test_recorded_gather_view_needs_an_even_attend_count(pkg, cuda):
+    """A gathered-slot view handed out while recording is a fixed address in
+    the graph, while every replay flips the device-side slot parity once per
+    gathered attention: a recording with such a view and an odd number of
+    gathered attentions is refused at graph_end; with an even number, a
+    recorded consumer of the view reads the right step's outputs on every
+    replay (checked over two replays against an unrecorded context)."""
+    import dataclasses
+
+    from solidattention_repro_b200 import workloads
+
+    w = dataclasses.replace(workloads.CONFIGS["cfg3"], name="gather-parity-test", layers=2,
+                            context_blocks=40, budget_blocks=10, hot_blocks=2)
+    plain, info = workloads.make_context(w, 16, cuda, seed=21)
+    side = torch.cuda.Stream(cuda)
+    with torch.cuda.stream(side):
+        rec, _ = workloads.make_context(w, 16, cuda, seed=21)
+    q, kv = workloads.decode_inputs(w, info, 5, cuda, seed=21)
+    own, _ = rec.gather_buffer(1)
+    rec.gather_attach(0, [own])
+    outs = rec.new_output()
+    torch.cuda.synchronize(cuda)
+    with pytest.raises(pkg.SparseKVError) as e:
+        with rec.record():
+            for s in range(5):
+                rec.step(q[s], kv[s], outs)
+                rec.gather_wait(view=(s == 4))
+    assert e.value.status == pkg.SA_ERR_UNSUPPORTED
+    # nothing of the refused recording ran; start the gather afresh
+    rec.gather_attach(0, [own])
+    dst = torch.empty((w.seqs, w.layers, w.query_heads, 128), dtype=torch.float16, device=cuda)
+    with torch.cuda.stream(side), rec.record():
+        for s in range(4):
+            rec.step(q[s], kv[s], outs)
+            view = rec.gather_wait(view=(s == 3))
+        dst.copy_(view)  # a recorded consumer of the last step's slot
+    for replay in range(2):
+        with torch.cuda.stream(side):
+            rec.graph_launch()
+        side.synchronize()
+        for s in range(4):
+            want = plain.step(q[s], kv[s])
+        plain.sync()
+        assert torch.equal(dst, want.view(dst.shape)), replay
+    for c in (rec, plain):
+        assert c.status_bits() == 0
+        c.close()
+
+
 def test_gather_wait_gives_up_and_reports_timeout(pkg, cuda):
     """A gather wait whose arrivals never come (a second wait after a single
     gathered attention: nothing will add the arrivals it expects) gives up at

@@ -94,3 +94,23 @@ def test_profile_traffic_lookup(bench, tmp_path, monkeypatch):
     assert bench.profile_traffic("select", "cfg3", 650_000_000) == 612000000 * 650 / 600
     assert bench.profile_traffic("select", "cfg3") == 612000000.0
     assert bench.profile_traffic("select", "cfg5") is None
+
+
+@pytest.mark.parametrize("steps,warmup", [(20, 5), (2000, 20), (1, 0), (32, 0), (33, 3), (7, 3)])
+def test_tail_prefill_puts_a_seal_at_the_end_of_the_timed_steps(workloads, steps, warmup):
+    """The bench pre-fills every open tail so that its last timed step seals
+    (a block seals on the step that appends its 32nd token), whatever the
+    step counts, and counts the seals of its timed window."""
+    t0 = workloads.tail_for_seal_at_end(steps, warmup)
+    assert 0 <= t0 < 32
+    # replay the lifecycle: tail length before step i is (t0 + i) mod 32
+    tail, sealed_at = t0, []
+    for i in range(warmup + steps):
+        tail += 1
+        if tail == 32:
+            sealed_at.append(i)
+            tail = 0
+    assert sealed_at and sealed_at[-1] == warmup + steps - 1
+    timed = [i for i in sealed_at if i >= warmup]
+    assert workloads.seal_steps(t0, warmup, steps) == len(timed) >= 1
+    assert len(timed) == (steps + 31 - 0) // 32 if steps >= 32 else len(timed) == 1

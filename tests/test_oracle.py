@@ -225,6 +225,60 @@ def test_cpu_step_port_equals_reference(port, ref):
     assert np.array_equal(a[0], b[0]) and np.array_equal(bits(a[1]), bits(b[1]))
 
 
+def _units_for(oracle_mod, pool, reps, q, tails_len, nb_list, qh, kh, grp, budget):
+    """Unit descriptors over per-(layer) block arrays [nb + 1][32][2][KH][D]."""
+    keep, units = [], (oracle_mod.Unit * (len(nb_list) * kh))()
+    ids = np.zeros((len(nb_list), kh, budget), np.int64)
+    out = np.zeros((len(nb_list), qh, 128), np.float32)
+    for i, nb in enumerate(nb_list):
+        for h in range(kh):
+            u = units[i * kh + h]
+            u.blocks, u.reps, u.query = pool[i].ctypes.data, reps[i].ctypes.data, q[i].ctypes.data
+            u.nb, u.tail_len, u.kv_head = nb, tails_len, h
+            u.ids_out = ids[i, h].ctypes.data
+            u.out = out[i, h * grp:(h + 1) * grp].ctypes.data
+    keep.append((pool, reps, q))
+    return units, ids, out, keep
+
+
+def test_cpu_unit_step_equals_layer_step(port, ref):
+    """The unit-list CPU step (units of sequence-layers with their own block
+    counts in one parallel loop) gives the layer step's ids and outputs, and
+    the reference's own build of it gives the same bits."""
+    import oracle as oracle_mod
+
+    rng = np.random.default_rng(8)
+    qh, kh, nb, tail = 8, 2, 20, 9
+    grp = qh // kh
+    tv = 2 * kh * 128
+    pools = [cases.fp16(rng, (nb + 1) * 32 * tv) for _ in range(2)]
+    reps = [rng.standard_normal((qh, nb, 128), dtype=np.float32) for _ in range(2)]
+    q = [rng.standard_normal((qh, 128), dtype=np.float32) for _ in range(2)]
+    want = port.sparse_step(np.concatenate(pools), np.stack([np.arange(nb, dtype=np.int32) + i * (nb + 1)
+                                                            for i in range(2)]),
+                            np.stack(reps), np.stack(q),
+                            np.array([nb, 2 * nb + 1], np.int32), tail, qh, kh, 128, 32, nb, 6, 1,
+                            2, cases.SCALE, 2)
+    for lib in (port, ref):
+        units, ids, out, _ = _units_for(oracle_mod, pools, reps, q, tail, [nb, nb], qh, kh, grp, 6)
+        lib.sparse_units(units, qh, kh, 128, 6, 1, 2, cases.SCALE, 3)
+        assert np.array_equal(ids, want[0]) and np.array_equal(bits(out), bits(want[1]))
+
+
+def test_per_block_reps_equal_single_block_builds(port, ref):
+    rng = np.random.default_rng(9)
+    qh, kh, blocks = 8, 2, 5
+    t = 32 * blocks
+    pq = cases.fp16(rng, qh * t * 128).view(np.float16).astype(np.float32).reshape(qh, t, 128)
+    kv = cases.fp16(rng, t * 2 * kh * 128).reshape(t, -1)
+    want = np.stack([port.build_representatives(np.ascontiguousarray(pq[:, b * 32:(b + 1) * 32]),
+                                                kv[b * 32:(b + 1) * 32], 32, qh, kh, 128, 32, 32,
+                                                4)[0][:, 0] for b in range(blocks)], axis=1)
+    for lib in (port, ref):
+        got = lib.build_reps_per_block(pq, kv, blocks, qh, kh, 128, 32, 4, 3)
+        assert np.array_equal(bits(got), bits(want))
+
+
 def _compare_prediction(predicted, oracle):
     """cpp/src/pipeline_main.cpp:686-717, transliterated: hits, misses (oracle
     order), replacement slots (slot order), and the corrected resident set."""

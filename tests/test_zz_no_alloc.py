@@ -66,3 +66,56 @@ def test_noalloc_refuses_problems_beyond_its_scratch(pkg, cuda):
                 torch.cuda.current_stream().cuda_stream)
     assert status == pkg.SA_ERR_CAPACITY
     assert "2 MiB" in pkg.load().sa_last_error().decode()
+
+
+def _bound_cases(pkg, qh, kh):
+    """Token counts (multiples of 32) whose workspace is the largest at or
+    below the 2 MiB array and the smallest above it, for this device's plan."""
+    size = pkg.load().sa_attention_workspace_size
+    below = above = None
+    for entries in list(range(1, 4096)) + list(range(4096, 40000, 3)):
+        need = size(entries * 32, qh, kh)
+        if need <= (2 << 20):
+            # inputs of at most ~1.3 GB for the case that runs
+            if entries < 20000 and (below is None or need >= below[1]):
+                below = (entries * 32, need)
+        elif above is None or need < above[1]:
+            above = (entries * 32, need)
+    return below, above
+
+
+def test_noalloc_at_its_scratch_bound(pkg, cuda):
+    """The largest workspace that fits the array runs and matches the
+    workspace entry point; the smallest that does not is refused, so a
+    capacity check off by the array's alignment slack would show here."""
+    fn = _noalloc(pkg)
+    qh, kh = 64, 8
+    below, above = _bound_cases(pkg, qh, kh)
+    assert below is not None and above is not None
+    stream = torch.cuda.current_stream().cuda_stream
+    tokens = below[0]
+    assert below[1] > (2 << 20) * 0.85  # close to the bound (the plan's partials come in steps)
+    gen = torch.Generator(device=cuda).manual_seed(tokens)
+    kv = torch.randn(tokens * 2 * kh * 128, generator=gen, device=cuda).half().view(torch.int16)
+    q = torch.randn(qh * 128, generator=gen, device=cuda)
+    want = pkg.attention(kv, q, tokens, qh, kh, 128, SCALE).float().cpu().numpy()
+    got = torch.empty(qh, 128, device=cuda)
+    status = fn(kv.data_ptr(), q.data_ptr(), tokens, qh, kh, 128, SCALE, got.data_ptr(), 0, stream)
+    assert status == 0, pkg.load().sa_last_error()
+    torch.cuda.synchronize()
+    got = got.cpu().numpy()
+    assert np.abs(got - want).max() <= 2e-5 and cosine(got, want) >= 0.999999
+    status = fn(kv.data_ptr(), q.data_ptr(), above[0], qh, kh, 128, SCALE, got.data_ptr(), 0,
+                stream)
+    assert status == pkg.SA_ERR_CAPACITY, (above, status)
+
+
+def test_noalloc_refuses_other_head_dims(pkg, cuda):
+    fn = _noalloc(pkg)
+    qh, kh, tokens = 16, 8, 64
+    kv = torch.zeros(tokens * 2 * kh * 64, dtype=torch.int16, device=cuda)
+    q = torch.zeros(qh * 64, device=cuda)
+    out = torch.empty(qh * 64, device=cuda)
+    status = fn(kv.data_ptr(), q.data_ptr(), tokens, qh, kh, 64, 0.125, out.data_ptr(), 0,
+                torch.cuda.current_stream().cuda_stream)
+    assert status == pkg.SA_ERR_UNSUPPORTED
