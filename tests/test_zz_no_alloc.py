@@ -99,13 +99,13 @@ def test_noalloc_at_its_scratch_bound(pkg, cuda):
     kv = torch.randn(tokens * 2 * kh * 128, generator=gen, device=cuda).half().view(torch.int16)
     q = torch.randn(qh * 128, generator=gen, device=cuda)
     want = pkg.attention(kv, q, tokens, qh, kh, 128, SCALE).float().cpu().numpy()
-    got = torch.empty(qh, 128, device=cuda)
-    status = fn(kv.data_ptr(), q.data_ptr(), tokens, qh, kh, 128, SCALE, got.data_ptr(), 0, stream)
+    out = torch.empty(qh, 128, device=cuda)
+    status = fn(kv.data_ptr(), q.data_ptr(), tokens, qh, kh, 128, SCALE, out.data_ptr(), 0, stream)
     assert status == 0, pkg.load().sa_last_error()
     torch.cuda.synchronize()
-    got = got.cpu().numpy()
+    got = out.cpu().numpy()
     assert np.abs(got - want).max() <= 2e-5 and cosine(got, want) >= 0.999999
-    status = fn(kv.data_ptr(), q.data_ptr(), above[0], qh, kh, 128, SCALE, got.data_ptr(), 0,
+    status = fn(kv.data_ptr(), q.data_ptr(), above[0], qh, kh, 128, SCALE, out.data_ptr(), 0,
                 stream)
     assert status == pkg.SA_ERR_CAPACITY, (above, status)
 
