@@ -417,6 +417,10 @@ SA_API sa_status sa_ctx_gather_buffer(sa_ctx* ctx, int32_t world, void** buf_out
 SA_API sa_status sa_ctx_gather_attach(sa_ctx* ctx, int32_t rank, void* const* peer_bufs);
 /* Enqueue the wait for the latest attention's outputs from every rank;
  * *gathered_out (nullable) = the slot holding them [seqs][layers][world*QH][D].
+ * A decode step (sa_ctx_step) of an attached context already waits for them
+ * in its own seal kernel, so after a step this call only returns the slot
+ * and launches nothing; after an attention of its own (sa_ctx_attend,
+ * sa_ctx_step_raw) it enqueues the wait kernel.
  * A wait that gives up sets SA_DEV_TIMEOUT in the status word. The slot
  * parity and the expected arrival count are kept on the device, so
  * attention + wait pairs recorded with sa_ctx_graph_begin replay correctly

@@ -138,13 +138,16 @@ struct sa_ctx {
   int gather_world = 0, gather_rank = -1;
   void** gather_peers = nullptr;  // device array [gather_world]
   uint64_t gather_attends = 0;
+  uint64_t gather_waited = 0;  // gathered attends whose wait has been enqueued
   // decode-step graph: recorded between sa_ctx_graph_begin and _end
   bool recording = false;
   uint64_t launches_before_recording = 0;
   uint64_t gather_attends_before_recording = 0;
+  uint64_t gather_waited_before_recording = 0;
   bool gather_view_recorded = false;  // a gathered-slot view was handed out while recording
   uint64_t graph_launches = 0;        // kernel launches one replay issues
   uint64_t graph_gather_attends = 0;  // gathered attends one replay issues
+  uint64_t graph_gather_waited = 0;   // and the waits it enqueues
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t graph_exec = nullptr;
 };
@@ -1029,7 +1032,16 @@ sa_status ctx_step(sa_ctx* c, const float* query, const void* kv_new, int32_t kv
   ++c->launches;
   CtxDev d = c->dev;
   d.status_mirror = status_mirror;
-  return launch_seal(d, 1, c->stream, true);
+  if (c->gather_peers) {
+    // the seal kernel also waits for every rank's outputs of this attention
+    d.gather_counter =
+        reinterpret_cast<const unsigned long long*>(c->gather_buf + c->gather_counter_bytes);
+    d.gather_epoch = reinterpret_cast<unsigned long long*>(c->gather_buf + c->gather_counter_bytes + 8);
+    d.gather_per_step = (unsigned long long)c->gather_world * c->num_sl * c->cfg.kv_heads;
+  }
+  st = launch_seal(d, 1, c->stream, true);
+  if (st == SA_OK && c->gather_peers) c->gather_waited = c->gather_attends;
+  return st;
 }
 
 // Device-side address of a pinned, mapped host buffer aligned to `align`
@@ -1109,6 +1121,7 @@ SA_API sa_status sa_ctx_graph_begin(sa_ctx* c) {
   c->recording = true;
   c->launches_before_recording = c->launches;
   c->gather_attends_before_recording = c->gather_attends;
+  c->gather_waited_before_recording = c->gather_waited;
   c->gather_view_recorded = false;
   return SA_OK;
 }
@@ -1123,6 +1136,8 @@ SA_API sa_status sa_ctx_graph_end(sa_ctx* c) {
   c->launches = c->launches_before_recording;
   const uint64_t recorded_attends = c->gather_attends - c->gather_attends_before_recording;
   c->gather_attends = c->gather_attends_before_recording;
+  const uint64_t recorded_waits = c->gather_waited - c->gather_waited_before_recording;
+  c->gather_waited = c->gather_waited_before_recording;
   cudaGraph_t graph = nullptr;
   SA_CUDA_TRY(cudaStreamEndCapture(c->stream, &graph));
   if (c->gather_view_recorded && recorded_attends % 2 == 1) {
@@ -1149,6 +1164,7 @@ SA_API sa_status sa_ctx_graph_end(sa_ctx* c) {
   c->graph_exec = exec;
   c->graph_launches = recorded;
   c->graph_gather_attends = recorded_attends;
+  c->graph_gather_waited = recorded_waits;
   return SA_OK;
 }
 
@@ -1160,6 +1176,7 @@ SA_API sa_status sa_ctx_graph_launch(sa_ctx* c) {
   SA_CUDA_TRY(cudaGraphLaunch(c->graph_exec, c->stream));
   c->launches += c->graph_launches;
   c->gather_attends += c->graph_gather_attends;
+  c->gather_waited += c->graph_gather_waited;
   return SA_OK;
 }
 
@@ -1301,6 +1318,7 @@ SA_API sa_status sa_ctx_gather_attach(sa_ctx* c, int32_t rank, void* const* peer
   SA_CUDA_TRY(cudaStreamSynchronize(c->stream));
   SA_CUDA_TRY(cudaMemset(c->gather_buf + c->gather_counter_bytes, 0, 16));
   c->gather_attends = 0;
+  c->gather_waited = 0;
   c->gather_rank = rank;
   return SA_OK;
 }
@@ -1310,13 +1328,18 @@ SA_API sa_status sa_ctx_gather_wait(sa_ctx* c, void** gathered_out) {
   if (!c->gather_peers) return fail(SA_ERR_INVALID_ARG, "gather_wait: gather not attached");
   if (c->gather_attends == 0) return fail(SA_ERR_INVALID_ARG, "gather_wait: no gathered attend yet");
   DeviceGuard guard(c->cfg.device);
-  const unsigned long long units = (unsigned long long)c->num_sl * c->cfg.kv_heads;
-  ++c->launches;
-  const sa_status st = launch_gather_wait(
-      reinterpret_cast<const unsigned long long*>(c->gather_buf + c->gather_counter_bytes),
-      reinterpret_cast<unsigned long long*>(c->gather_buf + c->gather_counter_bytes + 8),
-      c->gather_world * units, c->dev.status, c->stream);
-  if (st != SA_OK) return st;
+  if (c->gather_waited != c->gather_attends) {
+    // an attention of its own (sa_ctx_attend): enqueue its wait; a decode
+    // step's seal kernel has already enqueued the wait of the step's attention
+    const unsigned long long units = (unsigned long long)c->num_sl * c->cfg.kv_heads;
+    ++c->launches;
+    const sa_status st = launch_gather_wait(
+        reinterpret_cast<const unsigned long long*>(c->gather_buf + c->gather_counter_bytes),
+        reinterpret_cast<unsigned long long*>(c->gather_buf + c->gather_counter_bytes + 8),
+        c->gather_world * units, c->dev.status, c->stream);
+    if (st != SA_OK) return st;
+    c->gather_waited = c->gather_attends;
+  }
   if (gathered_out) {
     *gathered_out = c->gather_buf + ((c->gather_attends - 1) % 2) * c->gather_slot_bytes;
     if (c->recording) c->gather_view_recorded = true;

@@ -127,14 +127,16 @@ struct alignas(128) AttnSmem {
   int last_flag;
 };
 
+// spec_id: the selected id at slot e (loaded by the caller together with the
+// count, before knowing whether e holds a selected block).
 __device__ __forceinline__ void unit_entry(const AttnParams& p, int sl, int sgroup, int nsel,
-                                           int tail_len, int e, int* phys, int* ntok) {
+                                           int tail_len, int e, int spec_id, int* phys,
+                                           int* ntok) {
   *phys = 0;
   *ntok = 0;
   int r;
   if (e < nsel) {
-    const int logical =
-        p.sel_ids ? p.sel_ids[(sl * p.n_sel_groups + sgroup) * p.sel_stride + e] : e;
+    const int logical = p.sel_ids ? spec_id : e;
     if (p.table) {
       if (logical < 0 || logical >= p.table_stride) {
         raise_status(p.status, SA_DEV_BAD_BLOCK);
@@ -283,11 +285,14 @@ __device__ __forceinline__ void gather_push(const AttnParams& p, AttnSmem<G>& s,
   }
   vsync<virt_ctas<G>()>();
   if (vtid<virt_ctas<G>()>() == 0) {
-    __threadfence_system();
-    for (int r = 0; r < p.gather_world; ++r)
-      atomicAdd_system(reinterpret_cast<unsigned long long*>(
-                           reinterpret_cast<uint8_t*>(p.gather_peers[r]) + p.gather_counter_bytes),
-                       1ull);
+    // release pattern at system scope: the fence orders the CTA's stores
+    // (ordered before it by the barrier) before the relaxed arrivals
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    for (int r = 0; r < p.gather_world; ++r) {
+      const unsigned long long* ctr = reinterpret_cast<const unsigned long long*>(
+          reinterpret_cast<uint8_t*>(p.gather_peers[r]) + p.gather_counter_bytes);
+      asm volatile("red.relaxed.sys.global.add.u64 [%0], 1;" ::"l"(ctr) : "memory");
+    }
   }
 }
 
@@ -368,13 +373,17 @@ __global__ void __launch_bounds__(kThreads * virt_ctas<G>(), 1)
     const int sl = u / p.kv_heads;
     const int kvh = u - sl * p.kv_heads;
     const int sgroup = kvh / p.kv_per_sel_group;
-    int nsel = p.sel_count ? p.sel_count[sl * p.n_sel_groups + sgroup] : p.fixed_nsel;
+    // the count, the tail length and the id at this slot in one round of loads
+    const int spec_id = p.sel_ids && e < p.sel_stride
+                            ? __ldcg(p.sel_ids + (sl * p.n_sel_groups + sgroup) * p.sel_stride + e)
+                            : 0;
+    int nsel = p.sel_count ? __ldcg(p.sel_count + sl * p.n_sel_groups + sgroup) : p.fixed_nsel;
     nsel = max(0, min(nsel, p.sel_ids ? p.sel_stride : nsel));
-    int tail_len = p.tail_len ? p.tail_len[sl] : p.fixed_tail_len;
+    int tail_len = p.tail_len ? __ldcg(p.tail_len + sl) : p.fixed_tail_len;
     if (tail_len < kBlockTokens) tail_len += p.tail_pending;
     tail_len = max(0, min(tail_len, kBlockTokens));
     int phys, ntok;
-    unit_entry(p, sl, sgroup, nsel, tail_len, e, &phys, &ntok);
+    unit_entry(p, sl, sgroup, nsel, tail_len, e, spec_id, &phys, &ntok);
     s.ent_phys[i] = phys;
     s.ent_ntok[i] = (uint8_t)ntok;
   }
@@ -598,27 +607,47 @@ __global__ void __launch_bounds__(kThreads * virt_ctas<G>(), 1)
           }
         }
         vsync<virt_ctas<G>()>();
-        if (vtid<virt_ctas<G>()>() == 0) {
-          // the barrier orders the CTA's partial stores before this fence
-          __threadfence();
-          s.last_flag = atomicAdd(&p.counters[u], 1) == nparts - 1;
-          if (s.last_flag) __threadfence();
-        }
+        if (vtid<virt_ctas<G>()>() == 0)  // the barrier orders the partial stores before it
+          s.last_flag = arrive_acq_rel(&p.counters[u]) == nparts - 1;
         vsync<virt_ctas<G>()>();
         if (s.last_flag) {
           const float* parts = p.partial + (size_t)u * p.max_segments * G * kPartialStride;
+          // The partials' loads go out kMergeBatch at a time (a loop of
+          // dependent L2 round trips took ~7 us when a unit had 9 parts);
+          // they are still combined in range order.
+          constexpr int kMergeBatch = 8;
           for (int idx = vtid<virt_ctas<G>()>(); idx < G * kHeadDim; idx += kThreads) {
             const int g = idx / kHeadDim, d = idx % kHeadDim;
             float M = -INFINITY;
-            for (int k = 0; k < nparts; ++k)
-              M = fmaxf(M, __ldcg(parts + (k * G + g) * kPartialStride));
+            for (int k0 = 0; k0 < nparts; k0 += kMergeBatch) {
+              float mk[kMergeBatch];
+#pragma unroll
+              for (int b = 0; b < kMergeBatch; ++b)
+                mk[b] = k0 + b < nparts ? __ldcg(parts + ((k0 + b) * G + g) * kPartialStride)
+                                        : -INFINITY;
+#pragma unroll
+              for (int b = 0; b < kMergeBatch; ++b) M = fmaxf(M, mk[b]);
+            }
             float L = 0.f, o = 0.f;
             if (M != -INFINITY) {
-              for (int k = 0; k < nparts; ++k) {
-                const float* pk = parts + (k * G + g) * kPartialStride;
-                const float f = exp2f(__ldcg(pk) - M);
-                L += __ldcg(pk + 1) * f;
-                o += __ldcg(pk + 2 + d) * f;
+              for (int k0 = 0; k0 < nparts; k0 += kMergeBatch) {
+                float mk[kMergeBatch], lk[kMergeBatch], ok[kMergeBatch];
+#pragma unroll
+                for (int b = 0; b < kMergeBatch; ++b) {
+                  const float* pk = parts + ((k0 + b) * G + g) * kPartialStride;
+                  const bool in = k0 + b < nparts;
+                  mk[b] = in ? __ldcg(pk) : 0.f;
+                  lk[b] = in ? __ldcg(pk + 1) : 0.f;
+                  ok[b] = in ? __ldcg(pk + 2 + d) : 0.f;
+                }
+#pragma unroll
+                for (int b = 0; b < kMergeBatch; ++b) {
+                  if (k0 + b < nparts) {
+                    const float f = exp2f(mk[b] - M);
+                    L += lk[b] * f;
+                    o += ok[b] * f;
+                  }
+                }
               }
             }
             store_out<G>(p, s, out_base, idx, L > 0.f ? o / L : 0.f);
@@ -666,20 +695,7 @@ sa_status launch_g(const AttnParams& p, cudaStream_t stream) {
 __global__ void gather_wait_kernel(const unsigned long long* counter, unsigned long long* epoch,
                                    unsigned long long per_step, uint32_t* status) {
   if (threadIdx.x != 0) return;
-  const unsigned long long e = *reinterpret_cast<volatile unsigned long long*>(epoch);
-  const unsigned long long expected = (e + 1) * per_step;
-  const long long start = clock64();
-  for (;;) {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(counter) : "memory");
-    if (v >= expected) break;
-    if (clock64() - start > kWaitLimitCycles) {
-      raise_status(status, SA_DEV_TIMEOUT);
-      break;
-    }
-    __nanosleep(256);
-  }
-  *epoch = e + 1;
+  gather_wait_device(counter, epoch, per_step, status);
 }
 
 }  // namespace

@@ -44,6 +44,22 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// ---- arrival counters ----------------------------------------------------------
+
+// One arrival on a GPU-scope counter with acquire-release semantics; returns
+// the count before it. Called by one thread after a barrier: the CTA's
+// earlier stores are visible before the arrival, and an arriver that sees
+// the last count sees every earlier arriver's stores (one atomic round trip,
+// where a fence, the atomic and a second fence took three).
+__device__ __forceinline__ int arrive_acq_rel(int* counter) {
+  int prev;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+               : "=r"(prev)
+               : "l"(counter)
+               : "memory");
+  return prev;
+}
+
 // ---- conversions -----------------------------------------------------------
 
 __device__ __forceinline__ float h2f(uint16_t h) {
@@ -112,6 +128,31 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 // is visible; returns at once when the kernel was launched without the
 // programmatic-serialization attribute.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ---- KV-head-sharded gather ----------------------------------------------------
+
+// One thread: waits, bounded, until this rank's arrival counter holds the
+// arrivals of gather epoch + 1 (per_step per epoch), with system-scope
+// acquire, then advances the epoch (the next attention writes the other
+// slot). A wait that gives up raises SA_DEV_TIMEOUT and still advances.
+__device__ __forceinline__ void gather_wait_device(const unsigned long long* counter,
+                                                   unsigned long long* epoch,
+                                                   unsigned long long per_step, uint32_t* status) {
+  const unsigned long long e = *reinterpret_cast<volatile unsigned long long*>(epoch);
+  const unsigned long long expected = (e + 1) * per_step;
+  const long long start = clock64();
+  for (;;) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(counter) : "memory");
+    if (v >= expected) break;
+    if (clock64() - start > kWaitLimitCycles) {
+      raise_status(status, SA_DEV_TIMEOUT);
+      break;
+    }
+    __nanosleep(256);
+  }
+  *epoch = e + 1;
+}
 
 // ---- per-head RMS norm + rotary embedding (Qwen3 q/k norm) --------------------
 

@@ -76,6 +76,13 @@ struct CtxDev {
   int* seal_counters;  // [0] arrivals of the seal kernel's CTAs; [1] 1 when an append filled a tail (or found it full)
   uint32_t* status;
   uint32_t* status_mirror;  // device-mapped host word the seal commit copies status to (nullable)
+  // KV-head-sharded gather (gather_counter null = off): the seal kernel of a
+  // decode step also waits, bounded, until this rank's arrival counter holds
+  // (epoch + 1) * gather_per_step arrivals, then advances the epoch (the wait
+  // of sa_ctx_gather_wait, without a launch of its own).
+  const unsigned long long* gather_counter;
+  unsigned long long* gather_epoch;
+  unsigned long long gather_per_step;
   int num_sl, qh, kv_heads;
   int rep_window, rep_topk;
   float rep_scale;

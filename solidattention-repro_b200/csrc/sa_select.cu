@@ -530,13 +530,9 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
   __syncthreads();
   if (nchunks > 1) {
     if (threadIdx.x == 0) {
-      // the barrier orders the CTA's score stores before this fence
-      __threadfence();
-      ts.last = atomicAdd(&p.counters[unit], 1) == nchunks - 1;
-      if (ts.last) {
-        __threadfence();
-        p.counters[unit] = 0;
-      }
+      // the barrier orders the CTA's score stores before the arrival
+      ts.last = arrive_acq_rel(&p.counters[unit]) == nchunks - 1;
+      if (ts.last) p.counters[unit] = 0;
     }
     __syncthreads();
     if (!ts.last) return;

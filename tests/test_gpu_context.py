@@ -262,10 +262,13 @@ def test_kv_head_shards_reassemble_the_unsharded_step(pkg, cuda):
 
 def test_gather_over_peer_buffers_assembles_all_heads(pkg, cuda):
     """The attention epilogue's gather: two KV-head shards of one sequence
-    (emulated ranks on one GPU, one stream, so every wait is satisfied when it
-    runs) store their outputs into both ranks' gathered buffers; each buffer's
-    slot then holds the full head set, equal to the unsharded context's output,
-    for consecutive steps (alternating slots)."""
+    (emulated ranks on one GPU, one stream) store their outputs into both
+    ranks' gathered buffers; each buffer's slot then holds the full head set,
+    equal to the unsharded context's output, for consecutive steps
+    (alternating slots). The emulated ranks run the step's stages one call at
+    a time -- both attentions before either wait -- so every wait is already
+    satisfied when it runs (a decode step would wait inside its own seal
+    kernel for a rank queued behind it)."""
     import dataclasses
 
     from solidattention_repro_b200 import sharding, workloads
@@ -288,9 +291,14 @@ def test_gather_over_peer_buffers_assembles_all_heads(pkg, cuda):
     slots = set()
     for step in range(3):
         want = full.step(q[step], kv[step]).float().cpu().numpy()
-        locals_ = [ctx.step(qs[step], kvs[step]).float().cpu().numpy() for ctx, qs, kvs in ranks]
+        locals_ = []
+        for ctx, qs, kvs in ranks:
+            ctx.append(qs[step], kvs[step])
+            ctx.select(qs[step])
+            locals_.append(ctx.attend(qs[step]).float().cpu().numpy())
         for r, (ctx, _, _) in enumerate(ranks):
             got_t = ctx.gather_wait()
+            ctx.seal()
             ctx.sync()
             slots.add(got_t.data_ptr() - bufs[r])
             got = got_t.float().cpu().numpy()
@@ -392,11 +400,12 @@ def test_recorded_gather_view_needs_an_even_attend_count(pkg, cuda):
 
 
 def test_gather_wait_gives_up_and_reports_timeout(pkg, cuda):
-    """A gather wait whose arrivals never come (a second wait after a single
-    gathered attention: nothing will add the arrivals it expects) gives up at
-    its bounded limit (about a second) and reports SA_DEV_TIMEOUT in the
-    status word instead of hanging; the next synchronisation returns
-    SA_ERR_TIMEOUT."""
+    """A gather wait whose arrivals never come (a rank that never attends)
+    gives up at its bounded limit (about a second) and reports
+    SA_DEV_TIMEOUT in the status word instead of hanging; the next
+    synchronisation returns SA_ERR_TIMEOUT. Before that, a step's own wait
+    (in its seal kernel) and an explicit wait after a standalone attention
+    both pass."""
     import dataclasses
 
     from solidattention_repro_b200 import workloads
@@ -404,13 +413,23 @@ def test_gather_wait_gives_up_and_reports_timeout(pkg, cuda):
     w = dataclasses.replace(workloads.CONFIGS["cfg3"], name="gather-timeout-test", layers=1,
                             context_blocks=16, budget_blocks=8, hot_blocks=1)
     ctx, info = workloads.make_context(w, 4, cuda, seed=13)
-    q, kv = workloads.decode_inputs(w, info, 1, cuda, seed=13)
+    q, kv = workloads.decode_inputs(w, info, 2, cuda, seed=13)
     own, _ = ctx.gather_buffer(1)
     ctx.gather_attach(0, [own])
-    ctx.step(q[0], kv[0])
-    ctx.gather_wait(view=False)  # its arrivals are there
+    ctx.step(q[0], kv[0])         # the step's seal kernel waits: the arrivals are there
+    ctx.gather_wait(view=False)   # nothing left to wait for after a step
     assert ctx.sync() == 0
-    ctx.gather_wait(view=False)  # expects the arrivals of an attention that never runs
+    ctx.attend(q[0])              # an attention of its own ...
+    ctx.gather_wait(view=False)   # ... and its wait kernel
+    assert ctx.sync() == 0
+    ctx.close()
+    # a two-rank gather whose second rank never attends (its buffer is a
+    # plain allocation here): this rank's step waits for arrivals that never come
+    ctx, info = workloads.make_context(w, 4, cuda, seed=13)
+    own, nbytes = ctx.gather_buffer(2)
+    absent = torch.zeros(nbytes, dtype=torch.uint8, device=cuda)
+    ctx.gather_attach(0, [own, absent.data_ptr()])
+    ctx.step(q[1], kv[1])
     with pytest.raises(pkg.SparseKVError) as e:
         ctx.sync()
     assert e.value.status == pkg.SA_ERR_TIMEOUT
