@@ -553,11 +553,14 @@ def timed_steps(ctx, step, first, count, use_graph, stream, barrier):
         with torch.cuda.stream(stream), ctx.record():
             for s in range(first, first + count):
                 step(s)
+    # The sampler is running before the region starts; every rank starts its
+    # region after the barrier (a rank that started early would wait for the
+    # others' gathered outputs inside its own timed region).
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.wait_first()
     barrier()
     torch.cuda.synchronize()
     launches0 = ctx.launches
-    clocks = ClockSampler(torch.cuda.current_device())
-    clocks.wait_first()  # the sampler is running before the region starts
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
@@ -699,6 +702,23 @@ def our_arm(args, w, rank, world, local_rank, pkg):
     step_dist = {"p10": pct(per_step, 0.1), "p50": pct(per_step, 0.5), "p90": pct(per_step, 0.9),
                  "max": per_step[-1] if per_step else None, "steps": dist_steps, "unit": "ms",
                  "timing": "CUDA events between consecutive single-step calls, rank 0"}
+
+    # ---- the peer-memory gather against NCCL: one more step's gathered slot
+    # equals an NCCL all-gather of every rank's own output (bit for bit)
+    gather_check = None
+    if p2p:
+        with torch.cuda.stream(stream):
+            ctx.step(queries[W], kv_new[W], out)
+            got = ctx.gather_wait().clone()
+            ref = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device=dev)
+            dist.all_gather_into_tensor(ref, out)
+            ref = ref.permute(1, 2, 0, 3, 4).reshape(got.shape)
+            same = torch.equal(got, ref)
+        stream.synchronize()
+        gather_check = max_over_ranks(0.0 if same else 1.0) == 0.0
+        phase_bits["gather_check"] = ctx.status_bits()
+        ctx.sync()
+        barrier()
 
     # ---- per-kernel roofline: each kernel alone, on its launch stream
     q_last = queries[total - 1]
@@ -873,6 +893,7 @@ def our_arm(args, w, rank, world, local_rank, pkg):
             "quality": qual,
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": gpu_launches,
             "replicas": replicas,
+            "gather_equals_nccl_all_gather": gather_check,
             "reference_shapes": ref_shapes,
             "device_status_bits": phase_bits,
             "clocks": clock_info,

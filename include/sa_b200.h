@@ -395,10 +395,11 @@ SA_API sa_status sa_ctx_export_blocks(sa_ctx* ctx, int32_t seq, int32_t layer, i
  * attention launch of the context also stores each (seq-layer, KV head)
  * output into the current parity slot of every rank's gathered buffer
  * (NVLink P2P stores), laid out [seqs][layers][world*QH][D] (the full head
- * set), and counts one system-scope arrival per output on every rank's
- * buffer. sa_ctx_gather_wait enqueues a bounded wait for all ranks' outputs
- * of the latest attention. Slots alternate per attention, so a slot stays
- * valid until the attention after next.
+ * set). After the attention completes, one thread fences at system scope
+ * and counts one arrival on every rank's buffer, then waits, bounded, for
+ * every rank's arrival (in a decode step's own seal kernel, or in the
+ * kernel sa_ctx_gather_wait enqueues). Slots alternate per attention, so a
+ * slot stays valid until the attention after next.
  *
  * Setup, per rank: sa_ctx_gather_buffer -> sa_ipc_export the buffer ->
  * exchange the handles (any host channel) -> sa_ipc_open every other rank's

@@ -682,8 +682,10 @@ sa_status ctx_select(sa_ctx* c, const float* query, const void* kv_new = nullptr
 }
 
 // pending: tokens appended by a fused append this step, not yet in tail_len.
+// step_gather: the decode step's seal kernel signals the gather for the
+// whole grid (else every unit counts its own arrivals).
 sa_status ctx_attend(sa_ctx* c, const float* query, void* out, int pending = 0,
-                     bool pdl = false) {
+                     bool pdl = false, bool step_gather = false) {
   AttnParams p{};
   p.tail_pending = pending;
   p.pdl = pdl;
@@ -721,6 +723,7 @@ sa_status ctx_attend(sa_ctx* c, const float* query, void* out, int pending = 0,
     p.gather_counter_bytes = c->gather_counter_bytes;
     p.gather_epoch = reinterpret_cast<const unsigned long long*>(c->gather_buf +
                                                                  c->gather_counter_bytes + 8);
+    p.gather_unit_arrivals = step_gather ? 0 : 1;
   }
   ++c->launches;
   const sa_status st = launch_attention(p, c->stream);
@@ -1028,7 +1031,7 @@ sa_status ctx_step(sa_ctx* c, const float* query, const void* kv_new, int32_t kv
   // and cost 29 us per step on a B200, while the two links save 3.6 us.
   sa_status st;
   if ((st = ctx_select(c, query, kv_new, kv_fp32, false)) != SA_OK) return st;
-  if ((st = ctx_attend(c, query, out, 1, true)) != SA_OK) return st;
+  if ((st = ctx_attend(c, query, out, 1, true, true)) != SA_OK) return st;
   ++c->launches;
   CtxDev d = c->dev;
   d.status_mirror = status_mirror;
@@ -1037,7 +1040,9 @@ sa_status ctx_step(sa_ctx* c, const float* query, const void* kv_new, int32_t kv
     d.gather_counter =
         reinterpret_cast<const unsigned long long*>(c->gather_buf + c->gather_counter_bytes);
     d.gather_epoch = reinterpret_cast<unsigned long long*>(c->gather_buf + c->gather_counter_bytes + 8);
-    d.gather_per_step = (unsigned long long)c->gather_world * c->num_sl * c->cfg.kv_heads;
+    d.gather_peers = c->gather_peers;
+    d.gather_world = c->gather_world;
+    d.gather_counter_bytes = c->gather_counter_bytes;
   }
   st = launch_seal(d, 1, c->stream, true);
   if (st == SA_OK && c->gather_peers) c->gather_waited = c->gather_attends;
@@ -1316,7 +1321,7 @@ SA_API sa_status sa_ctx_gather_attach(sa_ctx* c, int32_t rank, void* const* peer
   // A fresh start: arrival counter and epoch zero (late arrivals of a step
   // whose wait timed out are dropped with them), slot parity even.
   SA_CUDA_TRY(cudaStreamSynchronize(c->stream));
-  SA_CUDA_TRY(cudaMemset(c->gather_buf + c->gather_counter_bytes, 0, 16));
+  SA_CUDA_TRY(cudaMemset(c->gather_buf + c->gather_counter_bytes, 0, 24));
   c->gather_attends = 0;
   c->gather_waited = 0;
   c->gather_rank = rank;
@@ -1331,12 +1336,13 @@ SA_API sa_status sa_ctx_gather_wait(sa_ctx* c, void** gathered_out) {
   if (c->gather_waited != c->gather_attends) {
     // an attention of its own (sa_ctx_attend): enqueue its wait; a decode
     // step's seal kernel has already enqueued the wait of the step's attention
-    const unsigned long long units = (unsigned long long)c->num_sl * c->cfg.kv_heads;
     ++c->launches;
     const sa_status st = launch_gather_wait(
+        c->gather_peers, c->gather_world, c->gather_counter_bytes,
         reinterpret_cast<const unsigned long long*>(c->gather_buf + c->gather_counter_bytes),
         reinterpret_cast<unsigned long long*>(c->gather_buf + c->gather_counter_bytes + 8),
-        c->gather_world * units, c->dev.status, c->stream);
+        (unsigned long long)c->gather_world * c->num_sl * c->cfg.kv_heads, c->dev.status,
+        c->stream);
     if (st != SA_OK) return st;
     c->gather_waited = c->gather_attends;
   }

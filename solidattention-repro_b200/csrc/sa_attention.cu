@@ -264,9 +264,13 @@ __device__ __forceinline__ void store_out(const AttnParams& p, AttnSmem<G>& s, s
 }
 
 // Copies unit u's staged output into every rank's gathered buffer (16-byte
-// P2P stores over NVLink; the own rank's buffer is local), then counts one
-// arrival on every rank's counter. The barrier orders all threads' stores
-// before thread 0's system-scope fence and atomics.
+// P2P stores over NVLink; the own rank's buffer is local). In a decode step
+// nothing else happens here: once the whole attention grid has completed,
+// one thread of the step's seal kernel fences once at system scope and
+// signals every rank (gather_signal_wait). A standalone attention also
+// counts the unit's arrival on every rank (one fence and one remote atomic
+// per rank for every unit: at eight GPUs that per-unit work was a large
+// part of the step).
 template <int G>
 __device__ __forceinline__ void gather_push(const AttnParams& p, AttnSmem<G>& s, int u) {
   vsync<virt_ctas<G>()>();
@@ -283,6 +287,7 @@ __device__ __forceinline__ void gather_push(const AttnParams& p, AttnSmem<G>& s,
     uint8_t* dst = reinterpret_cast<uint8_t*>(p.gather_peers[r]) + off + (size_t)c * 16;
     *reinterpret_cast<uint4*>(dst) = reinterpret_cast<const uint4*>(s.ostage)[c];
   }
+  if (!p.gather_unit_arrivals) return;
   vsync<virt_ctas<G>()>();
   if (vtid<virt_ctas<G>()>() == 0) {
     // release pattern at system scope: the fence orders the CTA's stores
@@ -692,17 +697,20 @@ sa_status launch_g(const AttnParams& p, cudaStream_t stream) {
 // epoch + 1, then advances the epoch: the next attention writes the other
 // slot. Epoch and expected count live on the device, so a recorded graph
 // replays them correctly.
-__global__ void gather_wait_kernel(const unsigned long long* counter, unsigned long long* epoch,
-                                   unsigned long long per_step, uint32_t* status) {
+__global__ void gather_wait_kernel(void* const* peers, int world, size_t counter_bytes,
+                                   const unsigned long long* counter, unsigned long long* epoch,
+                                   unsigned long long per_epoch, uint32_t* status) {
   if (threadIdx.x != 0) return;
-  gather_wait_device(counter, epoch, per_step, status);
+  gather_signal_wait(peers, world, counter_bytes, counter, epoch, per_epoch, false, status);
 }
 
 }  // namespace
 
-sa_status launch_gather_wait(const unsigned long long* counter, unsigned long long* epoch,
-                             unsigned long long per_step, uint32_t* status, cudaStream_t stream) {
-  gather_wait_kernel<<<1, 32, 0, stream>>>(counter, epoch, per_step, status);
+sa_status launch_gather_wait(void* const* peers, int world, size_t counter_bytes,
+                             const unsigned long long* counter, unsigned long long* epoch,
+                             unsigned long long per_epoch, uint32_t* status, cudaStream_t stream) {
+  gather_wait_kernel<<<1, 32, 0, stream>>>(peers, world, counter_bytes, counter, epoch, per_epoch,
+                                           status);
   return cuda_status(cudaGetLastError(), "gather_wait_kernel launch");
 }
 

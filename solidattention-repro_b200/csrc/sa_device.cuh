@@ -131,15 +131,38 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 
 // ---- KV-head-sharded gather ----------------------------------------------------
 
-// One thread: waits, bounded, until this rank's arrival counter holds the
-// arrivals of gather epoch + 1 (per_step per epoch), with system-scope
-// acquire, then advances the epoch (the next attention writes the other
-// slot). A wait that gives up raises SA_DEV_TIMEOUT and still advances.
-__device__ __forceinline__ void gather_wait_device(const unsigned long long* counter,
+// One thread, after a gathered attention grid has completed (every unit's
+// output stored into every rank's gathered slot). The gather buffer's
+// control words are [counter][epoch][target]: arrivals so far, gathers
+// completed, and the arrivals that complete the latest one.
+// signal: a decode step's seal kernel signals this rank's arrival to every
+// rank itself -- one system-scope fence, cumulative over the attention
+// grid's peer stores (which happen before its grid dependency wait), then
+// one relaxed arrival per rank -- and this gather expects `per_epoch` =
+// world arrivals; after a standalone attention, whose units each arrived on
+// every rank, it expects world * units and signals nothing.
+// Then it waits, bounded, with system-scope acquire loads, until the
+// counter reaches the target, and advances the epoch (the next attention
+// writes the other slot). A wait that gives up raises SA_DEV_TIMEOUT and
+// still advances the epoch.
+__device__ __forceinline__ void gather_signal_wait(void* const* peers, int world,
+                                                   size_t counter_bytes,
+                                                   const unsigned long long* counter,
                                                    unsigned long long* epoch,
-                                                   unsigned long long per_step, uint32_t* status) {
-  const unsigned long long e = *reinterpret_cast<volatile unsigned long long*>(epoch);
-  const unsigned long long expected = (e + 1) * per_step;
+                                                   unsigned long long per_epoch, bool signal,
+                                                   uint32_t* status) {
+  if (signal) {
+    asm volatile("fence.sc.sys;" ::: "memory");
+    for (int r = 0; r < world; ++r) {
+      const unsigned long long* ctr = reinterpret_cast<const unsigned long long*>(
+          reinterpret_cast<const uint8_t*>(peers[r]) + counter_bytes);
+      asm volatile("red.relaxed.sys.global.add.u64 [%0], 1;" ::"l"(ctr) : "memory");
+    }
+  }
+  unsigned long long* target = epoch + 1;
+  const unsigned long long expected = *reinterpret_cast<volatile unsigned long long*>(target) +
+                                      per_epoch;
+  *target = expected;
   const long long start = clock64();
   for (;;) {
     unsigned long long v;
@@ -149,9 +172,9 @@ __device__ __forceinline__ void gather_wait_device(const unsigned long long* cou
       raise_status(status, SA_DEV_TIMEOUT);
       break;
     }
-    __nanosleep(256);
+    __nanosleep(128);
   }
-  *epoch = e + 1;
+  *epoch = *reinterpret_cast<volatile unsigned long long*>(epoch) + 1;
 }
 
 // ---- per-head RMS norm + rotary embedding (Qwen3 q/k norm) --------------------

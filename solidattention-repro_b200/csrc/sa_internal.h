@@ -77,12 +77,14 @@ struct CtxDev {
   uint32_t* status;
   uint32_t* status_mirror;  // device-mapped host word the seal commit copies status to (nullable)
   // KV-head-sharded gather (gather_counter null = off): the seal kernel of a
-  // decode step also waits, bounded, until this rank's arrival counter holds
-  // (epoch + 1) * gather_per_step arrivals, then advances the epoch (the wait
-  // of sa_ctx_gather_wait, without a launch of its own).
+  // decode step also signals this rank's arrival to every rank and waits,
+  // bounded, for every rank's (gather_signal_wait with signal; the wait of
+  // sa_ctx_gather_wait, without a launch of its own).
   const unsigned long long* gather_counter;
   unsigned long long* gather_epoch;
-  unsigned long long gather_per_step;
+  void* const* gather_peers;  // device array [gather_world]
+  int gather_world;
+  size_t gather_counter_bytes;
   int num_sl, qh, kv_heads;
   int rep_window, rep_topk;
   float rep_scale;
@@ -139,6 +141,10 @@ struct AttnParams {
   size_t gather_slot_bytes;
   size_t gather_counter_bytes;
   const unsigned long long* gather_epoch;
+  // 1: every unit's push also counts an arrival on every rank (a standalone
+  // attention, waited for by sa_ctx_gather_wait); 0: the decode step's seal
+  // kernel signals once per rank for the whole grid
+  int gather_unit_arrivals;
 };
 
 // The persistent attention schedule: `ctas` CTAs, each owning a contiguous
@@ -152,10 +158,11 @@ struct AttnPlan {
 AttnPlan attention_plan(int units, int slots_per_unit, int group, int sms);
 size_t attention_scratch_bytes(const AttnPlan& plan, int units, int group);
 sa_status launch_attention(const AttnParams& p, cudaStream_t stream);
-// Waits (bounded, one thread) until *counter >= expected with system-scope
-// acquire; SA_DEV_TIMEOUT in *status when it gives up.
-sa_status launch_gather_wait(const unsigned long long* counter, unsigned long long* epoch,
-                             unsigned long long per_step, uint32_t* status, cudaStream_t stream);
+// One thread: gather_signal_wait (sa_device.cuh) after a standalone
+// gathered attention; SA_DEV_TIMEOUT in *status when the wait gives up.
+sa_status launch_gather_wait(void* const* peers, int world, size_t counter_bytes,
+                             const unsigned long long* counter, unsigned long long* epoch,
+                             unsigned long long per_epoch, uint32_t* status, cudaStream_t stream);
 
 // ---- selection (sa_select.cu) ----------------------------------------------------
 

@@ -386,10 +386,12 @@ __global__ void __launch_bounds__(kRepThreads, 3) seal_kernel(const CtxDev c, in
   __shared__ int last;
   pdl_launch_dependents();
   pdl_wait();  // the attention of this step still reads the tails
-  // A gathered step also waits here for every rank's outputs (CTA 0, before
-  // the commit and the status mirror, which its barriers order after it).
+  // A gathered step also signals and waits here for every rank's outputs
+  // (CTA 0, before the commit and the status mirror, which its barriers
+  // order after it).
   if (c.gather_counter && blockIdx.x == 0 && threadIdx.x == 0)
-    gather_wait_device(c.gather_counter, c.gather_epoch, c.gather_per_step, c.status);
+    gather_signal_wait(c.gather_peers, c.gather_world, c.gather_counter_bytes, c.gather_counter,
+                       c.gather_epoch, (unsigned long long)c.gather_world, true, c.status);
   if (pending && __ldcg(c.seal_counters + 1) == 0) {
     // The step's appends filled no tail (the fused append flags one that it
     // fills or finds full): only the tail lengths move, by one CTA.
