@@ -333,7 +333,8 @@ def run_cpu_baseline(ctx, w, q_step, seconds, cores):
         while time.perf_counter() < t_end or len(times) < 2:
             times.append(us.run(lib, w, ctx.qh, ctx.kh, threads))
         per_step = statistics.median(times) * units_total / len(us.pairs)
-        result[f"steps_per_s_{label}"] = 1.0 / per_step
+        # sequence-steps/s, as the GPU arm counts them
+        result[f"steps_per_s_{label}"] = ctx.seqs / per_step
         result[f"runs_{label}"] = len(times)
         ids = us.ids
         for k, (i, h) in enumerate(us.pairs):
@@ -874,8 +875,9 @@ def our_arm(args, w, rank, world, local_rank, pkg):
             "seals_in_timed_region": seals,
             "step_ms_distribution": step_dist,
             "selected_kv_gbs": attn_gbs, "selected_kv_frac": attn_gbs / hbm,
-            # selected KV (16-token average tail) per GPU-step x per-GPU steps/s
-            "step_selected_kv_gbs": w.selected_kv_bytes(16) * steps_per_s / world / 1e9,
+            # one GPU's selected KV of a step (16-token average tail) / the step time
+            "step_selected_kv_gbs": w.selected_kv_bytes(16) * (1 if shard == "seqs" else 1.0 / world)
+            / (ms / K * 1e-3) / 1e9,
             "roofline": {"bound": "hbm", "kernel": dominant[0], "achieved": dominant[2],
                          "peak": hbm, "unit": "GB/s", "frac": dominant[2] / hbm,
                          "peak_kind": peak_kind, "traffic": traffic,
