@@ -82,6 +82,9 @@ def parse_args():
                          "from the attention kernel (p2p) or an NCCL all-gather after it")
     ap.add_argument("--layers", type=int, default=None,
                     help="override the workload's layer count (small profiling cases)")
+    ap.add_argument("--rank-share", type=int, default=1,
+                    help="on one GPU, run rank 0's share of an N-GPU KV-head split (its KV "
+                         "heads of every layer, no gather): the per-rank work of --gpus N")
     return ap.parse_args()
 
 
@@ -172,6 +175,8 @@ def job_layout(args, w, world: int, rank: int):
     from solidattention_repro_b200 import sharding
 
     if world == 1:
+        if getattr(args, "rank_share", 1) > 1:
+            return "share", sharding.shard_kv_heads(w.kv_heads, args.rank_share, 0), 0
         return "single", None, 0
     shard = args.shard
     if shard == "auto":
@@ -190,6 +195,9 @@ def job_config(args, w, world: int, shard: str, initial_tail: int) -> dict:
                   else "an NCCL all-gather"))
     elif shard == "seqs":
         par = f"sequence-split x{world}, no data-path collective"
+    elif shard == "share":
+        par = (f"one rank's share of a kv-head split x{args.rank_share} "
+               f"(rank 0's KV heads, no gather), on one GPU")
     else:
         par = "single"
     return {
@@ -831,7 +839,7 @@ def our_arm(args, w, rank, world, local_rank, pkg):
     mass = ctx.audit(q_last)
     ctx.sync()
     hot = info["hot"]
-    if heads_mode:
+    if kv_slice is not None:
         hot = hot[:, :, kv_slice[0]:kv_slice[0] + kv_slice[1]]
     qual = quality_mod.selection_quality(
         mass.cpu().numpy(), ctx.selected.cpu().numpy(), ctx.selected_count.cpu().numpy(),
