@@ -287,6 +287,36 @@ class Port(_Lib):
                                   re.ctypes.data, st.ctypes.data, units, budget)
         return sl, mi, re, st
 
+    def dense_block_mass(self, keys, query, block_tokens, scale):
+        """audit_dense_selection's per-block mass (see sao_dense_block_mass):
+        keys [tokens][head_dim] FP16 (as uint16 or float16), query
+        [heads][head_dim] FP32; returns float64 [ceil(tokens / block_tokens)]."""
+        k = np.ascontiguousarray(keys).view(np.uint16) if np.asarray(keys).dtype == np.float16 \
+            else np.ascontiguousarray(keys, np.uint16)
+        tokens, d = k.shape
+        q = np.ascontiguousarray(query, np.float32).reshape(-1, d)
+        out = np.zeros(max(1, -(-tokens // block_tokens)), np.float64)
+        P = C.c_void_p
+        fn = self.lib.sao_dense_block_mass
+        fn.argtypes = [P, _sz, _sz, P, _sz, _sz, _sz, C.c_float, P]
+        fn.restype = None
+        fn(k.ctypes.data, d, tokens, q.ctypes.data, q.shape[0], d, block_tokens, float(scale),
+           out.ctypes.data)
+        return out[:-(-tokens // block_tokens)]
+
+    def audit_selection(self, block_mass, selected, budget, init, local, extra_mass=0.0):
+        """(selected_mass, recall) of one selection (see sao_audit_selection)."""
+        m = np.ascontiguousarray(block_mass, np.float64)
+        sel = np.ascontiguousarray(selected, np.int32).reshape(-1)
+        a, r = C.c_double(), C.c_double()
+        P = C.c_void_p
+        fn = self.lib.sao_audit_selection
+        fn.argtypes = [P, _sz, P, _sz, _sz, _sz, _sz, C.c_double, P, P]
+        fn.restype = None
+        fn(m.ctypes.data, m.size, sel.ctypes.data, sel.size, budget, init, local,
+           float(extra_mass), C.byref(a), C.byref(r))
+        return a.value, r.value
+
     def lifecycle_run(self, layers, q_heads, kv_heads, head_dim, block_tokens, local_tokens,
                       decode_tokens, initial_blocks, with_store=False, with_indices=False):
         class Res(C.Structure):

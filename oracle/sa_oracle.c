@@ -448,6 +448,73 @@ int sao_lifecycle_run(size_t layers, size_t q_heads, size_t kv_heads,
   return 0;
 }
 
+/* audit_dense_selection, dense part (cpp/src/pipeline_main.cpp:517-543): per
+ * head, logits[t] = (sequential FP32 dot) * scale; the FP32 maximum; each
+ * logit replaced by expf(logit - maximum) and summed into a double
+ * denominator; then block_mass[t / block_tokens] += p / denominator / heads in
+ * double, heads in index order. */
+void sao_dense_block_mass(const uint16_t* keys, size_t key_stride, size_t tokens,
+                          const float* query, size_t heads, size_t head_dim,
+                          size_t block_tokens, float scale, double* block_mass) {
+  const size_t blocks = (tokens + block_tokens - 1) / block_tokens;
+  for (size_t b = 0; b < blocks; ++b) block_mass[b] = 0.0;
+  float* logits = (float*)malloc((tokens ? tokens : 1) * sizeof(float));
+  for (size_t head = 0; head < heads; ++head) {
+    float maximum = -INFINITY;
+    for (size_t t = 0; t < tokens; ++t) {
+      float dot = 0.0f;
+      for (size_t d = 0; d < head_dim; ++d)
+        dot += query[head * head_dim + d] * sao_half_to_float(keys[t * key_stride + d]);
+      logits[t] = dot * scale;
+      if (logits[t] > maximum) maximum = logits[t];
+    }
+    double denominator = 0.0;
+    for (size_t t = 0; t < tokens; ++t) {
+      logits[t] = expf(logits[t] - maximum);
+      denominator += logits[t];
+    }
+    for (size_t t = 0; t < tokens; ++t)
+      block_mass[t / block_tokens] += logits[t] / denominator / (double)heads;
+  }
+  free(logits);
+}
+
+/* audit_dense_selection, figures (pipeline_main.cpp:544-569). The oracle set
+ * starts from the forced blocks (the reference's blocks 0 and 15) and takes
+ * blocks in stable descending mass order until it holds `budget`; walking
+ * that order and skipping members equals taking, `budget - forced` times, the
+ * highest-mass block not yet in the set, the lowest index among equals. */
+void sao_audit_selection(const double* block_mass, size_t blocks, const int32_t* selected,
+                         size_t count, size_t budget, size_t init, size_t local,
+                         double extra_mass, double* selected_mass, double* recall) {
+  unsigned char* chosen = (unsigned char*)calloc(blocks ? blocks : 1, 1);
+  size_t members = 0;
+  for (size_t b = 0; b < blocks; ++b) {
+    if (b < init || b + local >= blocks) {
+      chosen[b] = 1;
+      ++members;
+    }
+  }
+  while (members < budget && members < blocks) {
+    size_t best = blocks;
+    for (size_t b = 0; b < blocks; ++b)
+      if (!chosen[b] && (best == blocks || block_mass[b] > block_mass[best])) best = b;
+    chosen[best] = 1;
+    ++members;
+  }
+  double mass = 0.0;
+  size_t hits = 0;
+  for (size_t i = 0; i < count; ++i) {
+    const int32_t b = selected[i];
+    if (b < 0 || (size_t)b >= blocks) continue;
+    mass += block_mass[b];
+    hits += chosen[b];
+  }
+  *selected_mass = mass + extra_mass;
+  *recall = members ? (double)hits / (double)members : 0.0;
+  free(chosen);
+}
+
 uint64_t sao_fnv_offsets(const int64_t* values, size_t n) {
   uint64_t hash = 1469598103934665603ULL;
   for (size_t i = 0; i < n; ++i) {

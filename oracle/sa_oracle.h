@@ -182,6 +182,27 @@ void sao_slot_correct(const int32_t* selected, const int32_t* counts, int32_t* s
                       int32_t* misses, int32_t* replace, int32_t* stats, size_t units,
                       size_t budget);
 
+/* Dense per-block attention mass of audit_dense_selection
+ * (cpp/src/pipeline_main.cpp:517-543) for one dense token set: keys
+ * [tokens] rows of head_dim FP16 values, `key_stride` elements apart; query
+ * [heads][head_dim] FP32. Per head: FP32 logits (sequential dot, then
+ * * scale), the FP32 maximum, expf of the shifted logits, a double
+ * denominator; each token adds p / denominator / heads to
+ * block_mass[token / block_tokens] (double, zeroed here). */
+void sao_dense_block_mass(const uint16_t* keys, size_t key_stride, size_t tokens,
+                          const float* query, size_t heads, size_t head_dim,
+                          size_t block_tokens, float scale, double* block_mass);
+
+/* The audit's two figures for one selection (pipeline_main.cpp:544-569):
+ * selected_mass = the summed mass of the selected blocks plus `extra_mass`
+ * (the always-attended open tail); recall = hits / the oracle set's size,
+ * where the oracle set is the forced blocks ([0, init) and the last `local`
+ * of `blocks`) filled to `budget` from a stable descending sort of the mass.
+ * The reference's fixed case is blocks 16, init 1, local 1, budget 4. */
+void sao_audit_selection(const double* block_mass, size_t blocks, const int32_t* selected,
+                         size_t count, size_t budget, size_t init, size_t local,
+                         double extra_mass, double* selected_mass, double* recall);
+
 /* Per-head RMS norm then rotate-half RoPE on rows of 128 floats, in place:
  * head_rms (cpp/src/qwen_layer_main.cpp:146-161, pairwise sum of squares,
  * strides 64..1) and rope (:163-183) at one position. */

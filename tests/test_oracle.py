@@ -358,3 +358,71 @@ def test_head_norm_rope_matches_float64(port):
         # powf / cosf / sinf of the C library may round an ulp off numpy's
         np.testing.assert_allclose(got, want, rtol=1e-5,
                                    atol=(1e-5 + 2e-7 * pos) * np.abs(want).max())
+
+
+# ------------------------------------------ audit_dense_selection restatement
+
+def test_dense_block_mass_matches_float64(port):
+    """sao_dense_block_mass restates pipeline_main.cpp:517-543 (FP32 logits,
+    expf, double denominator) at the reference's own audit shape (512 tokens,
+    16 heads, 16 blocks of 32): within FP32 logit rounding of a float64
+    softmax, and its blocks sum to 1. A partial last block (an open tail)
+    takes the remaining tokens."""
+    rng = np.random.default_rng(5)
+    for tokens in (512, 300):
+        keys = rng.standard_normal((tokens, 128)).astype(np.float16)
+        q = rng.standard_normal((16, 128)).astype(np.float32)
+        m = port.dense_block_mass(keys, q, 32, 1.0 / np.sqrt(128.0))
+        lg = q.astype(np.float64) @ keys.astype(np.float64).T / np.sqrt(128.0)
+        p = np.exp(lg - lg.max(1, keepdims=True))
+        p /= p.sum(1, keepdims=True)
+        pad = np.zeros((16, -(-tokens // 32) * 32))
+        pad[:, :tokens] = p
+        want = pad.reshape(16, -1, 32).sum(2).mean(0)
+        assert m.shape == want.shape
+        np.testing.assert_allclose(m, want, rtol=2e-6)
+        assert abs(m.sum() - 1.0) < 1e-12
+
+
+def test_audit_selection_reference_case_and_product_quality(port, pkg):
+    """sao_audit_selection at the reference's fixed case (16 blocks, forced 0
+    and 15, budget 4: pipeline_main.cpp:544-569), including a tie that the
+    stable sort gives to the lower block; then the product's host figures
+    (quality.selection_quality) equal it unit by unit on random masses."""
+    from solidattention_repro_b200 import quality
+
+    m = np.full(16, 0.01)
+    m[[3, 6, 9]] = [0.2, 0.3, 0.2]  # 3 and 9 tie: 3 ranks first
+    sel_mass, recall = port.audit_selection(m, [0, 6, 9, 15], 4, 1, 1)
+    assert recall == 0.75  # oracle set {0, 15, 6, 3}
+    assert sel_mass == pytest.approx(0.01 + 0.3 + 0.2 + 0.01)
+    assert port.audit_selection(m, [0, 3, 6, 15], 4, 1, 1)[1] == 1.0
+
+    rng = np.random.default_rng(9)
+    n_sl, kh, groups, budget, init, local, table = 6, 4, 2, 6, 1, 2, 24
+    nb = rng.integers(4, table + 1, n_sl)
+    mass = np.zeros((n_sl, kh, table + 1))
+    selected = np.full((n_sl, groups, budget), -1, np.int32)
+    counts = np.zeros((n_sl, groups), np.int32)
+    for sl in range(n_sl):
+        for h in range(kh):
+            raw = rng.random(nb[sl] + 1)
+            raw /= raw.sum()
+            mass[sl, h, :nb[sl]] = raw[:-1]
+            mass[sl, h, -1] = raw[-1]
+        for g in range(groups):
+            c = min(budget, nb[sl])
+            selected[sl, g, :c] = np.sort(rng.choice(nb[sl], c, replace=False))
+            counts[sl, g] = c
+    got = quality.selection_quality(mass, selected, counts, nb, budget, init, local)
+    want_mass, want_recall = [], []
+    for sl in range(n_sl):
+        for h in range(kh):
+            g = h * groups // kh
+            a, r = port.audit_selection(mass[sl, h, :nb[sl]], selected[sl, g, :counts[sl, g]],
+                                        budget, init, local, mass[sl, h, -1])
+            want_mass.append(a)
+            want_recall.append(r)
+    assert got["units"] == n_sl * kh
+    assert got["selected_mass"] == pytest.approx(np.mean(want_mass), abs=1e-12)
+    assert got["oracle_recall"] == pytest.approx(np.mean(want_recall), abs=1e-12)
