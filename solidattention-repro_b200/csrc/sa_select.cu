@@ -52,9 +52,8 @@ constexpr int kTieMax = kThreads;  // threshold buckets this small are ranked di
 constexpr int kSmemKeyBlocks = 2048;
 
 struct TopkShared {
-  int hist[2][256];                 // radix histograms, double-buffered by pass
-  uint32_t cand_key[kTieMax];       // threshold-bucket members gathered for ranking
-  int cand_idx[kTieMax];
+  int hist[2][256];                      // digit histograms, double-buffered by pass
+  unsigned long long cand[kTieMax];      // threshold-bucket members, (key, ~index) packed
   int digit;
   int above;
   int bucket;
@@ -62,6 +61,15 @@ struct TopkShared {
   int warp_count[kWarps];
   int last;
 };
+
+// A bucket member's ranking word: larger = earlier in the reference's order
+// (score descending, then index ascending).
+__device__ __forceinline__ unsigned long long rank_word(uint32_t key, int i) {
+  return ((unsigned long long)key << 32) | (uint32_t)~(uint32_t)i;
+}
+__device__ __forceinline__ int rank_word_index(unsigned long long w) {
+  return (int)~(uint32_t)w;
+}
 
 // Representatives are read once per step: a read-only load that does not
 // allocate in L1 (on a B200 the select ran ~2 us faster with it).
@@ -285,22 +293,35 @@ __device__ void select_top_k(const SelectParams& p, int unit, int nb, const floa
       if (bucket == remaining) break;
       if (bucket <= kTieMax) {
         // gather the members (in any order) and rank each among them
-        for_keys([&](int i, uint32_t k) {
-          if (!forced(i) && (k & mask) == prefix) {
-            const int s = atomicAdd(&ts.ncand, 1);
-            ts.cand_key[s] = k;
-            ts.cand_idx[s] = i;
+        // (one shared-memory atomic per warp and 32 blocks: with many equal
+        // keys the members crowd into few warps)
+        constexpr int kGatherBatch = kSmemKeys ? 4 : 16;  // key loads in flight together
+        for (int base = 0; base < nb; base += kThreads * kGatherBatch) {
+          uint32_t k[kGatherBatch];
+#pragma unroll
+          for (int u = 0; u < kGatherBatch; ++u) {
+            const int i = base + u * kThreads + tid;
+            k[u] = i < nb ? key_at(i) : 0u;
           }
-        });
+#pragma unroll
+          for (int u = 0; u < kGatherBatch; ++u) {
+            const int i = base + u * kThreads + tid;
+            const bool m = i < nb && !forced(i) && (k[u] & mask) == prefix;
+            const uint32_t b = __ballot_sync(kFull, m);
+            int slot = 0;
+            if (lane == 0 && b) slot = atomicAdd(&ts.ncand, __popc(b));
+            slot = __shfl_sync(kFull, slot, 0);
+            if (m) ts.cand[slot + __popc(b & lanes_below)] = rank_word(k[u], i);
+          }
+        }
         __syncthreads();
         if (tid < bucket) {
-          const uint32_t k = ts.cand_key[tid];
-          const int i = ts.cand_idx[tid];
+          // a packed word per member: one compare of the (key, index) order
+          const unsigned long long mine = ts.cand[tid];
           int rank = 0;
-          for (int j = 0; j < bucket; ++j) {
-            const uint32_t kj = ts.cand_key[j];
-            rank += kj > k || (kj == k && ts.cand_idx[j] < i);
-          }
+#pragma unroll 4
+          for (int j = 0; j < bucket; ++j) rank += ts.cand[j] > mine;
+          const int i = rank_word_index(mine);
           if (rank < remaining) atomicOr(&tie_bits[i >> 5], 1u << (i & 31));
         }
         __syncthreads();

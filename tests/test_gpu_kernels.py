@@ -134,12 +134,17 @@ def test_select_signed_zero_and_equal_scores(pkg, port, cuda):
 
 
 @pytest.mark.parametrize("blocks", [1200, 5000])  # order keys in shared memory / from L2
-@pytest.mark.parametrize("case", ["crowded_bucket", "infinite_score", "two_values"])
+@pytest.mark.parametrize("case", ["crowded_bucket", "infinite_score", "two_values",
+                                  "nested_scales"])
 def test_select_top_k_adversarial_scores(pkg, port, cuda, case, blocks):
-    """Adversarial score sets for the radix top-k: two far outliers above
-    near-equal scores, an infinite score, and scores of only two values (more
-    equal keys at the threshold than can be ranked directly)."""
-    rng = np.random.default_rng({"crowded_bucket": 1, "infinite_score": 2, "two_values": 3}[case])
+    """Adversarial score sets for the top-k: two far outliers above
+    near-equal scores (a second bucket level), an infinite score (an
+    overflowing range), scores of only two values (more equal keys at the
+    threshold than can be ranked directly), and outliers nested at four
+    scales above near-equal scores (more bucket levels than the linear
+    select takes, so the radix select finishes)."""
+    rng = np.random.default_rng({"crowded_bucket": 1, "infinite_score": 2, "two_values": 3,
+                                 "nested_scales": 4}[case])
     qh, budget = 4, 100
     q = rng.standard_normal((qh, 128), dtype=np.float32)
     base = rng.standard_normal((qh, 1, 128), dtype=np.float32)
@@ -152,6 +157,9 @@ def test_select_top_k_adversarial_scores(pkg, port, cuda, case, blocks):
         reps[:, 900] *= -1e4
         if case == "infinite_score":
             reps[:, 33] = np.float32(1e30) * np.sign(q)
+        if case == "nested_scales":
+            for b, f in ((11, 1e6), (12, 3e3), (13, 3.0), (14, 1e6), (15, 3e3)):
+                reps[:, b] *= np.float32(f)
     reps = np.ascontiguousarray(reps.astype(np.float32))
     want, _ = port.select_grouped(q, reps, qh, qh, blocks, 128, budget, 1, 2)
     ids, _ = pkg.select_shared_blocks(_t(q, cuda), _t(reps, cuda), qh, blocks, 128, budget, 1, 2)
