@@ -19,11 +19,11 @@
 //
 // Pipeline: a stage holds two entries of one segment (2 x 16 KB: the K rows
 // then the V rows of the unit's KV head, 32 x 256 B each) in a ring of three
-// stages. Every lane reads only its own sixteen-byte column of its own rows
-// (below), so every lane also loads exactly those bytes itself, with 16-byte
-// cp.async copies through the load/store unit, one commit group per stage: a
-// lane waits only for its own copies and refills its part of a stage as soon
-// as it has computed on it, with no producer thread and no cross-warp release.
+// stages. Every warp reads only its own rows (below), so its lanes load
+// exactly those rows themselves, with 16-byte cp.async copies through the
+// load/store unit, one commit group per stage: a warp waits only for its own
+// copies and refills its part of a stage as soon as it has computed on it,
+// with no producer thread and no cross-warp release.
 // (On a B200, streaming random 16 KB blocks: one thread per SM issuing 16 KB
 // bulk copies read at most 4.3 TB/s and two such threads per SM 6.6 TB/s,
 // whatever the number of copies in flight, while 16-byte cp.async copies
@@ -31,13 +31,22 @@
 // context's head-major pool or from a caller's token-major rows; the
 // shared-memory layout is the same.
 //
-// Warp w, per stage: half-warp h takes entry h of the stage and its tokens
-// [4w, 4w+4); lane l covers head dims [8(l%16), 8(l%16)+8). A quarter-warp
-// reads 128 contiguous bytes of one row: conflict-free. QK uses packed FP32
-// FMA (__ffma2_rn) with the softmax scale folded into q, then a 16-lane
-// transpose-reduce leaves one (token, head) logit per lane. The warp keeps an
-// FP32 online softmax per head (exp2 domain, running max shared by both
-// half-warps) and skips the accumulator rescale when no running max moved.
+// Warp w, per stage: rows [4w, 4w + 4) of both entries, 8 token rows, which
+// are also exactly the rows its lanes copy (so a warp waits only for its own
+// copies). The products run on the tensor cores (mma.sync, FP16 operands,
+// FP32 accumulation) with FP32-level accuracy: the FP32 query and the FP32
+// probabilities enter as FP16 hi + lo pairs (each pre-scaled by a power of
+// two), K and V are FP16 already, so every product is exact and the two
+// parts carry about 22 bits. S^T (8 rows x 8 head columns) = K . q^T takes
+// 16 m16n8k16 MMAs (A from ldmatrix, q^T held in registers for the
+// segment); the FP32 online softmax (exp2 domain, running max per head over
+// the warp's rows, rescaled lazily: only when a logit exceeds it by 2^8)
+// works on the accumulator fragments; movmatrix turns the probabilities into
+// the P^T operand, and O^T (128 dims x 8 head columns) += V^T . P^T takes 16
+// m16n8k8 MMAs (A from ldmatrix.trans). Per lane and stage that is ~110
+// instructions where FP32 FMAs on converted FP16 pairs took ~300. Shared
+// memory holds chunk c of warp-local row r at chunk c ^ r (conflict-free
+// ldmatrix); rows past an entry's token count are zeroed.
 //
 // At the end of a segment the eight warps merge by log-sum-exp through the
 // segment's last stage buffer, which is released only afterwards. A unit
@@ -106,8 +115,6 @@ __device__ __forceinline__ void vsync() {
 template <int G>
 struct alignas(128) AttnSmem {
   uint8_t tiles[kStages][kStageBytes];
-  float2 pbuf[kConsumerWarps][2][4][G];  // probabilities (p, p) [half][token][head]
-  float2 abuf[kConsumerWarps][G];        // rescale factor (a, a) per head
   float wscale[kConsumerWarps][G];
   float mw[kConsumerWarps][G];           // warp softmax states at a segment end
   float lw[kConsumerWarps][G];
@@ -174,54 +181,87 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-// In-warp transpose-reduce over lane bits OFF, OFF/2, ...: at each level a
-// lane keeps positions [0, M/2) of its M values and adds its partner's
-// positions [M/2, M). Each lane computes its values in an order XOR-permuted
-// by its own lane bits, so both partners' kept and received positions name
-// the same (token, head) pair and no selects are needed.
-template <int M, int OFF>
-struct Halve {
-  __device__ __forceinline__ static void run(float* a) {
-    if constexpr (M > 1 && OFF >= 1) {
-#pragma unroll
-      for (int j = 0; j < M / 2; ++j) a[j] += __shfl_xor_sync(kFull, a[j + M / 2], OFF);
-      Halve<M / 2, OFF / 2>::run(a);
-    }
-  }
-};
-
-__device__ __forceinline__ void unpack8(const uint4& u, float2 (&f)[4]) {
-  f[0] = h2x2f(u.x);
-  f[1] = h2x2f(u.y);
-  f[2] = h2x2f(u.z);
-  f[3] = h2x2f(u.w);
+// ---- tensor-core fragments (mma.sync, FP16 operands, FP32 accumulation) ----
+//
+// A warp owns 8 rows of a stage: tokens [t0, t0 + 4) of entry 0 (rows 0-3)
+// and of entry 1 (rows 4-7). In shared memory the 16-byte chunk c of row r
+// lives at chunk c ^ r, so the 8 row addresses of one ldmatrix fall into 8
+// different bank groups.
+__device__ __forceinline__ uint32_t smem_u32(const void* ptr) {
+  return (uint32_t)__cvta_generic_to_shared(ptr);
 }
 
-// G duplicated pairs from shared memory with the widest loads.
-template <int G>
-__device__ __forceinline__ void load_pairs(const float2* src, float2 (&v)[G]) {
-  if constexpr (G == 1) {
-    v[0] = src[0];
-  } else {
-#pragma unroll
-    for (int g = 0; g < G; g += 2) {
-      const float4 t = *reinterpret_cast<const float4*>(src + g);
-      v[g] = make_float2(t.x, t.y);
-      v[g + 1] = make_float2(t.z, t.w);
-    }
-  }
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
 }
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// d += A (16 x 16, rows 8-15 zero: a1 = a3 = 0) * B (16 x 8)
+__device__ __forceinline__ void mma_k16_top(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0,
+                                            uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+      "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+
+// d += A (16 x 8) * B (8 x 8)
+__device__ __forceinline__ void mma_k8(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+      "{%4, %5}, {%6}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(b0));
+}
+
+// The transpose of an 8 x 8 matrix of 16-bit values held one pair per lane.
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// (x, y) as FP16 hi + lo pairs: x = hi.x + lo.x to about 2^-22 relative.
+__device__ __forceinline__ void split_f16x2(float x, float y, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(x, y);
+  const float2 hf = __half22float2(h);
+  hi = h2_bits(h);
+  lo = h2_bits(__floats2half2_rn(x - hf.x, y - hf.y));
+}
+
+// 2^e as a float, e in [-126, 127].
+__device__ __forceinline__ float exp2_int(int e) { return __int_as_float((e + 127) << 23); }
 
 // This lane's copies for stage j into shared-memory stage `slot`: rows
-// [t0, t0 + 4) of entry `half`, K then V plane, 16 bytes at column l16 --
-// exactly the bytes the lane reads; rows at or past the entry's token count
-// are not copied (the compute masks them).
+// [t0, t0 + 4) of entry `half`, K then V plane, the 16 bytes of chunk l16
+// (placed at chunk l16 ^ r for the warp-local row r = 4 half + row). Rows at
+// or past the entry's token count are zeroed instead: the MMAs multiply
+// them by zero probabilities, and stale bytes there could be NaN patterns.
 template <int G, bool kHeadMajor>
 __device__ __forceinline__ void load_stage(AttnSmem<G>& s, const AttnParams& p, int j, int slot,
                                            int half, int t0, int l16) {
   const uint32_t w = s.stage_info[j];
   const int ntok = info_ntok(w, half);
-  if (ntok <= t0) return;
+  uint8_t* dst = s.tiles[slot] + half * kEntryBytes + t0 * kRowBytes;
+  if (ntok <= t0) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int c = (l16 ^ (4 * half + r)) * 16;
+      *reinterpret_cast<uint4*>(dst + r * kRowBytes + c) = make_uint4(0u, 0u, 0u, 0u);
+      *reinterpret_cast<uint4*>(dst + kPlaneBytes + r * kRowBytes + c) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    return;
+  }
   const int phys = s.ent_phys[info_e0(w) + half];
   const int kvh = s.seg_unit[info_seg(w)] % p.kv_heads;
   const uint8_t* src;
@@ -238,12 +278,15 @@ __device__ __forceinline__ void load_stage(AttnSmem<G>& s, const AttnParams& p, 
     plane = (size_t)p.kv_heads * kRowBytes;
   }
   src += l16 * 16;
-  uint8_t* dst = s.tiles[slot] + half * kEntryBytes + t0 * kRowBytes + l16 * 16;
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
+    uint8_t* d = dst + r * kRowBytes + (l16 ^ (4 * half + r)) * 16;
     if (t0 + r < ntok) {
-      cp_async16(dst + r * kRowBytes, src + r * row_stride);
-      cp_async16(dst + kPlaneBytes + r * kRowBytes, src + plane + r * row_stride);
+      cp_async16(d, src + r * row_stride);
+      cp_async16(d + kPlaneBytes, src + plane + r * row_stride);
+    } else {
+      *reinterpret_cast<uint4*>(d) = make_uint4(0u, 0u, 0u, 0u);
+      *reinterpret_cast<uint4*>(d + kPlaneBytes) = make_uint4(0u, 0u, 0u, 0u);
     }
   }
 }
@@ -301,33 +344,9 @@ __device__ __forceinline__ void gather_push(const AttnParams& p, AttnSmem<G>& s,
   }
 }
 
-// acc[g] += p(token, g) * v(token) over the half-warp's 4 tokens; tokens at
-// or past ntok are skipped when kMasked (their rows may hold stale data).
-template <int G, bool kMasked>
-__device__ __forceinline__ void pv_tokens(const uint8_t* vrow, const float2 (*pb)[G], int t0,
-                                          int ntok, float2 (&acc)[G][4]) {
-#pragma unroll
-  for (int tt = 0; tt < 4; ++tt) {
-    if (!kMasked || t0 + tt < ntok) {
-      float2 v[4];
-      unpack8(*reinterpret_cast<const uint4*>(vrow + tt * kRowBytes), v);
-      float2 pp[G];
-      load_pairs<G>(pb[tt], pp);
-#pragma unroll
-      for (int g = 0; g < G; ++g)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) acc[g][c] = __ffma2_rn(pp[g], v[c], acc[g][c]);
-    }
-  }
-}
-
 template <int G, bool kHeadMajor>
 __global__ void __launch_bounds__(kThreads * virt_ctas<G>(), 1)
     attention_kernel(const AttnParams p) {
-  // Pairs (token, head) per half-warp: 4G over 16 lanes -> VPL per lane.
-  constexpr int NPH = 4 * G;
-  constexpr int VPL = NPH > 16 ? NPH / 16 : 1;
-  constexpr int kPairShift = NPH >= 16 ? 0 : (NPH == 8 ? 1 : 2);  // lanes per pair = 1 << shift
   extern __shared__ __align__(128) uint8_t smem_raw[];
   if (vbid<virt_ctas<G>()>() >= p.ctas) return;  // the idle half of an odd plan
   AttnSmem<G>& s = *reinterpret_cast<AttnSmem<G>*>(
@@ -406,18 +425,21 @@ __global__ void __launch_bounds__(kThreads * virt_ctas<G>(), 1)
   vsync<virt_ctas<G>()>();
   const int nstages = s.nstages;
 
-  const int half = lane >> 4;      // which entry of the stage
-  const int l16 = lane & 15;       // 16 B (8 dims) column of a 256 B row
+  const int half = lane >> 4;      // the entry this lane copies
+  const int l16 = lane & 15;       // the 16-byte chunk of a 256-byte row it copies
   const int t0 = 4 * warp;
-  // This lane's reduced (token, head) pairs after QK: v = pair0 + i, with
-  // v = token * G + head. QK runs in the order v ^ pair0 (see Halve): token
-  // tt reads row tt ^ tsw, head g uses q of head g ^ gsw.
-  const int pair0 = (l16 >> kPairShift) * VPL;
-  const int tsw = pair0 / G;
-  const int gsw = pair0 % G;
-  const bool pair_writer = (l16 & ((1 << kPairShift) - 1)) == 0;
-  // Byte offsets of this lane's 16 B column in its entry's K plane, per token.
-  const int col_off = half * kEntryBytes + t0 * kRowBytes + l16 * 16;
+  // MMA fragment coordinates: row group g (a token row of the warp, or a
+  // head for the q and P^T operands), pair t (heads 2t, 2t + 1 of the
+  // logits and the accumulators).
+  const int g = lane >> 2, t = lane & 3;
+  // ldmatrix: lane L gives the address of row L & 7 of matrix L >> 3.
+  const int lr = lane & 7;
+  const uint32_t row_off = (uint32_t)((lr >> 2) * kEntryBytes + (t0 + (lr & 3)) * kRowBytes);
+  // chunk 4 kk + (lane >> 3) of row lr sits at chunk_off(kk)
+  auto chunk_off = [&](int kk) { return (uint32_t)(((4 * kk + (lane >> 3)) ^ lr) * 16); };
+  // logit row g is token t0 + (g & 3) of entry g >> 2
+  const int my_tok = t0 + (g & 3);
+  const int my_ent = g >> 2;
   // one commit group per stage, the first kStages in flight before the loop
 #pragma unroll
   for (int j = 0; j < kStages; ++j) {
@@ -425,145 +447,157 @@ __global__ void __launch_bounds__(kThreads * virt_ctas<G>(), 1)
     cp_async_commit();
   }
 
-  float m_run[VPL], m_thr[VPL], l_run[VPL];
-  float2 acc[G][4];
-  float2 q[G][4];  // q[g] holds head g ^ gsw
+  // per head 2t + i: running max (log2 units), lazy-rescale threshold, sum of
+  // this lane's row's probabilities
+  float m_run[2], m_thr[2], l_run[2];
+  float acc[8][4];       // O^T: dims 16 m + g (+ 8) x heads 2t, 2t + 1, probabilities x 2^7
+  uint32_t qh[8][2], ql[8][2];  // q^T fragments of head g, hi and lo FP16 parts
+  float q_unscale = 1.f;        // logits = MMA result * q_unscale
   int stage = 0;
 
   for (int j = 0; j < nstages; ++j) {
     const uint32_t info = s.stage_info[j];
     if (info & kInfoStart) {
-      // ---- a new segment: its unit's q (scaled into the exp2 domain), fresh state ----
-      const float* qbase = p.query + (size_t)s.seg_unit[info_seg(info)] * G * kHeadDim + 8 * l16;
+      // ---- a new segment: its unit's q in the exp2 domain, scaled by a power
+      // of two so that its largest element is in [2^14, 2^15), split into
+      // FP16 hi + lo parts; fresh softmax state ----
+      const float* qrow = p.query + ((size_t)s.seg_unit[info_seg(info)] * G + g) * kHeadDim + 2 * t;
+      float2 qv[8][2];
+      uint32_t amax = 0u;
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float* qh = qbase + (g ^ gsw) * kHeadDim;
-        const float4 a = __ldg(reinterpret_cast<const float4*>(qh));
-        const float4 b = __ldg(reinterpret_cast<const float4*>(qh + 4));
-        q[g][0] = make_float2(a.x * p.scale_log2, a.y * p.scale_log2);
-        q[g][1] = make_float2(a.z * p.scale_log2, a.w * p.scale_log2);
-        q[g][2] = make_float2(b.x * p.scale_log2, b.y * p.scale_log2);
-        q[g][3] = make_float2(b.z * p.scale_log2, b.w * p.scale_log2);
+      for (int k = 0; k < 8; ++k) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) acc[g][c] = make_float2(0.f, 0.f);
+        for (int h = 0; h < 2; ++h) {
+          float2 v = make_float2(0.f, 0.f);
+          if (g < G) v = __ldg(reinterpret_cast<const float2*>(qrow + 16 * k + 8 * h));
+          v.x *= p.scale_log2;
+          v.y *= p.scale_log2;
+          qv[k][h] = v;
+          amax = max(amax, max(__float_as_uint(fabsf(v.x)), __float_as_uint(fabsf(v.y))));
+        }
       }
+      amax = __reduce_max_sync(kFull, amax);
+      const int e = amax == 0u ? 0 : (int)((amax >> 23) & 0xff) - 127;
+      const int qe = max(-100, min(100, 14 - e));
+      const float up = exp2_int(qe);
+      q_unscale = exp2_int(-qe);
 #pragma unroll
-      for (int i = 0; i < VPL; ++i) {
+      for (int k = 0; k < 8; ++k)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          split_f16x2(qv[k][h].x * up, qv[k][h].y * up, qh[k][h], ql[k][h]);
+#pragma unroll
+      for (int m = 0; m < 8; ++m)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[m][c] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
         m_run[i] = -INFINITY;
         m_thr[i] = -INFINITY;
         l_run[i] = 0.f;
       }
     }
     cp_async_wait<kStages - 1>();  // this lane's copies of stage j have landed
-    const int ntok = info_ntok(info, half);
-    const int ntok_other = info_ntok(info, half ^ 1);
-    const uint8_t* tile = s.tiles[stage];
-    if (t0 < ntok || t0 < ntok_other) {
-      const uint8_t* kcol = tile + col_off;
-      // ---- QK over this lane's 8 dims, 4 tokens x G heads (permuted order) ----
-      float part[NPH];
+    __syncwarp();                  // ... and the other lanes' (ldmatrix reads them)
+    const int ntok0 = info_ntok(info, 0);
+    const int ntok1 = info_ntok(info, 1);
+    if (t0 < ntok0 || t0 < ntok1) {
+      const uint32_t kbase = smem_u32(s.tiles[stage]) + row_off;
+      // ---- S^T (8 token rows x 8 heads) = K rows . q^T, hi and lo parts ----
+      // four independent accumulation chains (hi / lo x even / odd k-steps)
+      float sh0[4] = {0.f, 0.f, 0.f, 0.f}, sh1[4] = {0.f, 0.f, 0.f, 0.f};
+      float sl0[4] = {0.f, 0.f, 0.f, 0.f}, sl1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int tt = 0; tt < 4; ++tt) {
-        float2 k[4];
-        unpack8(*reinterpret_cast<const uint4*>(kcol + (tt ^ tsw) * kRowBytes), k);
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          float2 a = __fmul2_rn(q[g][0], k[0]);
-          a = __ffma2_rn(q[g][1], k[1], a);
-          a = __ffma2_rn(q[g][2], k[2], a);
-          a = __ffma2_rn(q[g][3], k[3], a);
-          part[tt * G + g] = a.x + a.y;
-        }
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t a[4];
+        ldsm_x4(kbase + chunk_off(kk), a);
+        mma_k16_top(sh0, a[0], a[1], qh[2 * kk][0], qh[2 * kk][1]);
+        mma_k16_top(sh1, a[2], a[3], qh[2 * kk + 1][0], qh[2 * kk + 1][1]);
+        mma_k16_top(sl0, a[0], a[1], ql[2 * kk][0], ql[2 * kk][1]);
+        mma_k16_top(sl1, a[2], a[3], ql[2 * kk + 1][0], ql[2 * kk + 1][1]);
       }
-      Halve<NPH, 8>::run(part);
-      if constexpr (NPH < 16) {
-#pragma unroll
-        for (int off = 1 << (kPairShift - 1); off >= 1; off >>= 1)
-          part[0] += __shfl_xor_sync(kFull, part[0], off);
-      }
-      // ---- online softmax over 8 tokens (4 per half-warp) per head, lazily
-      // rescaled: the running max moves only when a logit exceeds it by more
-      // than kLazyRescale (log2 units), so probabilities stay below
-      // 2^kLazyRescale and most stages skip the max reduction and rescale ----
-      float x[VPL];
-      bool over = false;
-#pragma unroll
-      for (int i = 0; i < VPL; ++i) {
-        const int tt = (pair0 + i) / G;
-        x[i] = (t0 + tt < ntok) ? part[i] : -INFINITY;
-        over |= x[i] > m_thr[i];
-      }
-      const bool rescale = __any_sync(kFull, over);
+      const bool valid = my_tok < (my_ent ? ntok1 : ntok0);
+      float x[2];
+      x[0] = valid ? ((sh0[0] + sh1[0]) + (sl0[0] + sl1[0])) * q_unscale : -INFINITY;
+      x[1] = valid ? ((sh0[1] + sh1[1]) + (sl0[1] + sl1[1])) * q_unscale : -INFINITY;
+      // ---- online softmax over the warp's 8 rows per head, lazily rescaled:
+      // the running max moves only when a logit exceeds it by more than
+      // kLazyRescale (log2 units), so probabilities stay below 2^kLazyRescale ----
+      const bool rescale = __any_sync(kFull, x[0] > m_thr[0] || x[1] > m_thr[1]);
       if (rescale) {
+        float alpha[2];
 #pragma unroll
-        for (int i = 0; i < VPL; ++i) {
+        for (int i = 0; i < 2; ++i) {
           float bm = fmaxf(x[i], __shfl_xor_sync(kFull, x[i], 4));
           bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 8));
           bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, 16));
           const float m_new = fmaxf(m_run[i], bm);
-          const float alpha = m_new == -INFINITY ? 1.f : fast_exp2(m_run[i] - m_new);
+          alpha[i] = m_new == -INFINITY ? 1.f : fast_exp2(m_run[i] - m_new);
           m_run[i] = m_new;
           m_thr[i] = m_new + kLazyRescale;
-          l_run[i] *= alpha;
-          const int v = pair0 + i;
-          if (pair_writer && half == 0 && v / G == 0) s.abuf[warp][v % G] = make_float2(alpha, alpha);
+          l_run[i] *= alpha[i];
+        }
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          acc[m][0] *= alpha[0];
+          acc[m][1] *= alpha[1];
+          acc[m][2] *= alpha[0];
+          acc[m][3] *= alpha[1];
         }
       }
+      float pr[2];
 #pragma unroll
-      for (int i = 0; i < VPL; ++i) {
-        const float pr = x[i] == -INFINITY ? 0.f : fast_exp2(x[i] - m_run[i]);
-        l_run[i] += pr;
-        const int v = pair0 + i;
-        if (pair_writer) s.pbuf[warp][half][v / G][v % G] = make_float2(pr, pr);
+      for (int i = 0; i < 2; ++i) {
+        pr[i] = x[i] == -INFINITY ? 0.f : fast_exp2(x[i] - m_run[i]);
+        l_run[i] += pr[i];
       }
-      __syncwarp();
-      // ---- PV over the half-warp's 4 tokens ----
-      if (rescale) {
-        float2 aa[G];
-        load_pairs<G>(s.abuf[warp], aa);
+      // ---- P^T operand: (row g, heads 2t, 2t+1) pairs, scaled by 2^7 and split
+      // into FP16 hi + lo, transposed to (rows 2t, 2t+1, head g) ----
+      uint32_t ph, pl;
+      split_f16x2(pr[0] * 128.f, pr[1] * 128.f, ph, pl);
+      ph = movmatrix_trans(ph);
+      pl = movmatrix_trans(pl);
+      // ---- O^T (128 dims x 8 heads) += V^T . P^T ----
+      const uint32_t vbase = kbase + kPlaneBytes;
 #pragma unroll
-        for (int g = 0; g < G; ++g)
-#pragma unroll
-          for (int c = 0; c < 4; ++c) acc[g][c] = __fmul2_rn(acc[g][c], aa[g]);
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t v[4];
+        ldsm_x4_trans(vbase + chunk_off(kk), v);
+        mma_k8(acc[2 * kk], v[0], v[1], ph);
+        mma_k8(acc[2 * kk], v[0], v[1], pl);
+        mma_k8(acc[2 * kk + 1], v[2], v[3], ph);
+        mma_k8(acc[2 * kk + 1], v[2], v[3], pl);
       }
-      const uint8_t* vrow = tile + col_off + kPlaneBytes;
-      if (ntok >= kBlockTokens) pv_tokens<G, false>(vrow, s.pbuf[warp][half], t0, ntok, acc);
-      else pv_tokens<G, true>(vrow, s.pbuf[warp][half], t0, ntok, acc);
-      __syncwarp();
     }
+    __syncwarp();  // the warp's ldmatrix reads of this stage are done before its refill
 
     if (info & kInfoEnd) {
       // ---- segment end: merge the 8 warps through this stage's buffer ----
       vsync<virt_ctas<G>()>();  // every warp is done reading the stage
       float* accw = reinterpret_cast<float*>(s.tiles[stage]);  // [8][G][128]
-      // the two half-warps hold different tokens of the same dims
+      // l of each head summed over the warp's 8 rows (the lanes sharing t)
 #pragma unroll
-      for (int g = 0; g < G; ++g)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          acc[g][c].x += __shfl_xor_sync(kFull, acc[g][c].x, 16);
-          acc[g][c].y += __shfl_xor_sync(kFull, acc[g][c].y, 16);
-        }
-      // l of each head summed over the warp's 8 token slots
-#pragma unroll
-      for (int i = 0; i < VPL; ++i) {
+      for (int i = 0; i < 2; ++i) {
         float ls = l_run[i] + __shfl_xor_sync(kFull, l_run[i], 4);
         ls += __shfl_xor_sync(kFull, ls, 8);
         ls += __shfl_xor_sync(kFull, ls, 16);
-        const int v = pair0 + i;
-        if (pair_writer && half == 0 && v / G == 0) {
-          s.mw[warp][v % G] = m_run[i];
-          s.lw[warp][v % G] = ls;
+        const int h = 2 * t + i;
+        if (g == 0 && h < G) {
+          s.mw[warp][h] = m_run[i];
+          s.lw[warp][h] = ls;
         }
       }
-      if (half == 0) {
+      // the warp's O^T fragments, back to unscaled probabilities
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-          float* dst = &accw[(warp * G + g) * kHeadDim + 8 * l16];
-          *reinterpret_cast<float4*>(dst) =
-              make_float4(acc[g][0].x, acc[g][0].y, acc[g][1].x, acc[g][1].y);
-          *reinterpret_cast<float4*>(dst + 4) =
-              make_float4(acc[g][2].x, acc[g][2].y, acc[g][3].x, acc[g][3].y);
+      for (int i = 0; i < 2; ++i) {
+        const int h = 2 * t + i;
+        if (h < G) {
+          float* dst = &accw[(warp * G + h) * kHeadDim + g];
+#pragma unroll
+          for (int m = 0; m < 8; ++m) {
+            dst[16 * m] = acc[m][i] * (1.f / 128.f);
+            dst[16 * m + 8] = acc[m][2 + i] * (1.f / 128.f);
+          }
         }
       }
       vsync<virt_ctas<G>()>();
