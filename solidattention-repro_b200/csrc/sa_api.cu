@@ -990,7 +990,10 @@ SA_API sa_status sa_ctx_select(sa_ctx* c, const float* query) {
 SA_API sa_status sa_ctx_attend(sa_ctx* c, const float* query, void* out) {
   if (!c || !query || !out) return fail(SA_ERR_INVALID_ARG, "attend: null argument");
   DeviceGuard guard(c->cfg.device);
-  return ctx_attend(c, query, out);
+  // A programmatic dependent of whatever kernel precedes it on the stream, as
+  // in a decode step: before griddepcontrol.wait the kernel reads no global
+  // memory, so only its launch overlaps the predecessor's last CTAs.
+  return ctx_attend(c, query, out, 0, true);
 }
 
 SA_API sa_status sa_ctx_seal(sa_ctx* c) {
