@@ -291,6 +291,49 @@ __device__ __forceinline__ void load_stage(AttnSmem<G>& s, const AttnParams& p, 
   }
 }
 
+// One plane (0: K rows, 1: V rows) of load_stage's copies. Loading a stage
+// plane by plane (all K rows, then all V rows) instead of row by row ran the
+// attention faster on plans with one whole unit per virtual CTA and about a
+// full wave (on a B200, 288 units of 129 slots: 99.5 -> 93.1 us; of 257
+// slots: 197 -> 180 us) and slower on the others (224 units on 224 virtual
+// CTAs: 43.5 -> 49.9 us; 2,304 units on 296: 376 -> 429 us).
+template <int G, bool kHeadMajor>
+__device__ __forceinline__ void load_plane(AttnSmem<G>& s, const AttnParams& p, int j, int slot,
+                                           int pl, int half, int t0, int l16) {
+  const uint32_t w = s.stage_info[j];
+  const int ntok = info_ntok(w, half);
+  uint8_t* dst = s.tiles[slot] + half * kEntryBytes + pl * kPlaneBytes + t0 * kRowBytes;
+  if (ntok <= t0) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+      *reinterpret_cast<uint4*>(dst + r * kRowBytes + (l16 ^ (4 * half + r)) * 16) =
+          make_uint4(0u, 0u, 0u, 0u);
+    return;
+  }
+  const int phys = s.ent_phys[info_e0(w) + half];
+  const int kvh = s.seg_unit[info_seg(w)] % p.kv_heads;
+  const uint8_t* src;
+  size_t row_stride;
+  if constexpr (kHeadMajor) {
+    src = reinterpret_cast<const uint8_t*>(p.pool) +
+          ((size_t)phys * p.kv_heads + kvh) * kEntryBytes + (size_t)pl * kPlaneBytes +
+          (size_t)t0 * kRowBytes;
+    row_stride = kRowBytes;
+  } else {
+    src = reinterpret_cast<const uint8_t*>(p.rows) +
+          ((size_t)phys * kBlockTokens + t0) * (size_t)p.row_bytes +
+          (size_t)(pl * p.kv_heads + kvh) * kRowBytes;
+    row_stride = (size_t)p.row_bytes;
+  }
+  src += l16 * 16;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    uint8_t* d = dst + r * kRowBytes + (l16 ^ (4 * half + r)) * 16;
+    if (t0 + r < ntok) cp_async16(d, src + r * row_stride);
+    else *reinterpret_cast<uint4*>(d) = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
 // Stores output element idx of unit u (local layout) and, when gathering,
 // stages it for the peer stores.
 template <int G>
@@ -344,7 +387,7 @@ __device__ __forceinline__ void gather_push(const AttnParams& p, AttnSmem<G>& s,
   }
 }
 
-template <int G, bool kHeadMajor>
+template <int G, bool kHeadMajor, bool kPlaneOrder>
 __global__ void __launch_bounds__(kThreads * virt_ctas<G>(), 1)
     attention_kernel(const AttnParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -443,7 +486,14 @@ __global__ void __launch_bounds__(kThreads * virt_ctas<G>(), 1)
   // one commit group per stage, the first kStages in flight before the loop
 #pragma unroll
   for (int j = 0; j < kStages; ++j) {
-    if (j < nstages) load_stage<G, kHeadMajor>(s, p, j, j, half, t0, l16);
+    if (j < nstages) {
+      if constexpr (kPlaneOrder) {
+        load_plane<G, kHeadMajor>(s, p, j, j, 0, half, t0, l16);
+        load_plane<G, kHeadMajor>(s, p, j, j, 1, half, t0, l16);
+      } else {
+        load_stage<G, kHeadMajor>(s, p, j, j, half, t0, l16);
+      }
+    }
     cp_async_commit();
   }
 
@@ -501,8 +551,10 @@ __global__ void __launch_bounds__(kThreads * virt_ctas<G>(), 1)
     __syncwarp();                  // ... and the other lanes' (ldmatrix reads them)
     const int ntok0 = info_ntok(info, 0);
     const int ntok1 = info_ntok(info, 1);
-    if (t0 < ntok0 || t0 < ntok1) {
-      const uint32_t kbase = smem_u32(s.tiles[stage]) + row_off;
+    const bool active = t0 < ntok0 || t0 < ntok1;
+    const uint32_t kbase = smem_u32(s.tiles[stage]) + row_off;
+    float x[2] = {-INFINITY, -INFINITY};
+    if (active) {
       // ---- S^T (8 token rows x 8 heads) = K rows . q^T, hi and lo parts ----
       // four independent accumulation chains (hi / lo x even / odd k-steps)
       float sh0[4] = {0.f, 0.f, 0.f, 0.f}, sh1[4] = {0.f, 0.f, 0.f, 0.f};
@@ -517,9 +569,13 @@ __global__ void __launch_bounds__(kThreads * virt_ctas<G>(), 1)
         mma_k16_top(sl1, a[2], a[3], ql[2 * kk + 1][0], ql[2 * kk + 1][1]);
       }
       const bool valid = my_tok < (my_ent ? ntok1 : ntok0);
-      float x[2];
       x[0] = valid ? ((sh0[0] + sh1[0]) + (sl0[0] + sl1[0])) * q_unscale : -INFINITY;
       x[1] = valid ? ((sh0[1] + sh1[1]) + (sl0[1] + sl1[1])) * q_unscale : -INFINITY;
+    }
+    // (QK and the softmax + PV in two blocks around a warp barrier: on a
+    // B200 the per-rank share of eight GPUs ran 20.4 -> 19.6 us)
+    __syncwarp();
+    if (active) {
       // ---- online softmax over the warp's 8 rows per head, lazily rescaled:
       // the running max moves only when a logit exceeds it by more than
       // kLazyRescale (log2 units), so probabilities stay below 2^kLazyRescale ----
@@ -700,22 +756,30 @@ __global__ void __launch_bounds__(kThreads * virt_ctas<G>(), 1)
 
     // Refill this lane's part of the stage with stage j + kStages (after a
     // segment end only now: the merge used the stage as scratch).
-    if (j + kStages < nstages) load_stage<G, kHeadMajor>(s, p, j + kStages, stage, half, t0, l16);
+    if (j + kStages < nstages) {
+      if constexpr (kPlaneOrder) {
+        load_plane<G, kHeadMajor>(s, p, j + kStages, stage, 0, half, t0, l16);
+        load_plane<G, kHeadMajor>(s, p, j + kStages, stage, 1, half, t0, l16);
+      } else {
+        load_stage<G, kHeadMajor>(s, p, j + kStages, stage, half, t0, l16);
+      }
+    }
     cp_async_commit();
     if (++stage == kStages) stage = 0;
   }
   cp_async_wait<0>();  // only empty groups remain; nothing lands after exit
 }
 
-template <int G, bool kHeadMajor>
+template <int G, bool kHeadMajor, bool kPlaneOrder>
 sa_status launch_layout(const AttnParams& p, cudaStream_t stream) {
   constexpr int kV = virt_ctas<G>();
   const size_t smem = kV * sizeof(AttnSmem<G>);
   static int configured[kMaxDevices];
-  const sa_status st =
-      ensure_smem_limit((const void*)attention_kernel<G, kHeadMajor>, (int)smem, configured);
+  const sa_status st = ensure_smem_limit((const void*)attention_kernel<G, kHeadMajor, kPlaneOrder>,
+                                         (int)smem, configured);
   if (st != SA_OK) return st;
-  const cudaError_t e = launch_kernel(attention_kernel<G, kHeadMajor>, dim3((p.ctas + kV - 1) / kV),
+  const cudaError_t e = launch_kernel(attention_kernel<G, kHeadMajor, kPlaneOrder>,
+                                      dim3((p.ctas + kV - 1) / kV),
                                       dim3(kThreads * kV),
                                       smem, stream, p.pdl != 0, p);
   if (e != cudaSuccess) return cuda_status(e, "attention_kernel launch");
@@ -724,7 +788,16 @@ sa_status launch_layout(const AttnParams& p, cudaStream_t stream) {
 
 template <int G>
 sa_status launch_g(const AttnParams& p, cudaStream_t stream) {
-  return p.head_major ? launch_layout<G, true>(p, stream) : launch_layout<G, false>(p, stream);
+  // stage loads plane by plane (load_plane) when every virtual CTA takes one
+  // whole unit and they fill about a wave
+  const long long units = (long long)p.num_sl * p.kv_heads;
+  const long long wave = (long long)device_sm_count() * virt_ctas<G>();
+  const bool plane_order = units == p.ctas && (long long)p.ctas * 10 >= wave * 9;
+  if (p.head_major)
+    return plane_order ? launch_layout<G, true, true>(p, stream)
+                       : launch_layout<G, true, false>(p, stream);
+  return plane_order ? launch_layout<G, false, true>(p, stream)
+                     : launch_layout<G, false, false>(p, stream);
 }
 
 // Waits (bounded) until this rank's counter holds the arrivals of gather
