@@ -85,6 +85,10 @@ def parse_args():
     ap.add_argument("--rank-share", type=int, default=1,
                     help="on one GPU, run rank 0's share of an N-GPU KV-head split (its KV "
                          "heads of every layer, no gather): the per-rank work of --gpus N")
+    ap.add_argument("--probe-streaming", action="store_true",
+                    help="instead of the decode step: stream random 16 KB pool entries into "
+                         "shared memory with per-lane cp.async and with bulk copies "
+                         "(sa_probe_stream) and print the GB/s of each")
     return ap.parse_args()
 
 
@@ -914,6 +918,55 @@ def our_arm(args, w, rank, world, local_rank, pkg):
         dist.destroy_process_group()
 
 
+def probe_streaming(args, pkg):
+    """The attention's two ways of staging entries, alone: one launch reads
+    `entries` distinct random 16 KB entries of a 1 GiB pool (more than L2),
+    CUDA events around `steps` back-to-back launches after `warmup`."""
+    import ctypes as C
+
+    import torch
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lib = pkg.load()
+    pool_entries, entries = 1 << 16, 288 * 128  # cfg3's selected entries of a step
+    pool = torch.zeros(pool_entries * 16384, dtype=torch.uint8, device=dev)
+    g = torch.Generator().manual_seed(1)
+    ids = torch.randperm(pool_entries, generator=g)[:entries].to(torch.int32).to(dev)
+    sink = torch.zeros(1024, dtype=torch.int64, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    steps, warmup = max(1, min(args.steps, 50)), max(3, min(args.warmup, 10))
+    out = {"probe": "streaming", "entry_bytes": 16384, "entries": entries,
+           "pool_bytes": pool_entries * 16384, "ctas_per_sm": 2, "threads": 256,
+           "stages": "3 x 32 KB", "steps": steps, "warmup": warmup}
+    for mode, name in ((0, "cp_async"), (1, "bulk")):
+        def launch():
+            rc = lib.sa_probe_stream(C.c_void_p(pool.data_ptr()), pool_entries,
+                                     C.c_void_p(ids.data_ptr()), entries, mode,
+                                     C.c_void_p(sink.data_ptr()), C.c_void_p(status.data_ptr()),
+                                     C.c_void_p(stream.cuda_stream))
+            if rc != 0:
+                raise RuntimeError(f"sa_probe_stream: {lib.sa_last_error().decode()}")
+        for _ in range(warmup):
+            launch()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            launch()
+        e1.record(stream)
+        e1.synchronize()
+        us = 1000.0 * e0.elapsed_time(e1) / steps
+        out[name] = {"us_per_launch": us, "gbs": entries * 16384 / (us * 1e-6) / 1e9}
+    out["status"] = int(status.item())
+    hbm, kind = peaks()
+    out["peak_gbs"] = hbm
+    out["peak_kind"] = kind
+    print(json.dumps(out), flush=True)
+
+
 def main():
     args = parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -923,6 +976,9 @@ def main():
     import __graft_entry__
 
     pkg = __graft_entry__.load_package()
+    if args.probe_streaming:
+        probe_streaming(args, pkg)
+        return
     from solidattention_repro_b200 import workloads
 
     w = workloads.CONFIGS[args.config]

@@ -437,6 +437,23 @@ SA_API sa_status sa_ipc_export(int32_t device, const void* dev_ptr, void* handle
 SA_API sa_status sa_ipc_open(int32_t device, const void* handle, void** dev_ptr_out);
 SA_API sa_status sa_ipc_close(int32_t device, void* dev_ptr);
 
+/* ---- streaming probe (no reference counterpart: a measurement aid) ----
+ * Reads entries of 16 KB (one (block, KV head) of the head-major pool) into
+ * shared memory the two ways the attention could stage them, two CTAs of
+ * 256 threads per SM each streaming a contiguous share of `entry_ids` through
+ * three 32 KB stages: mode 0 per-lane 16-byte cp.async copies (the
+ * attention's loads), mode 1 one 16 KB cp.async.bulk per entry issued by one
+ * thread and completed on an mbarrier (plain loads of this GPU's memory, no
+ * cluster multicast). pool: device, 16-byte aligned, pool_entries * 16384
+ * bytes; entry_ids: device [n] (ids outside the pool read entry 0);
+ * sink: device, at least SA_PROBE_SINK_WORDS uint64 (one word per CTA keeps
+ * the reads); status: device word or null (SA_DEV_TIMEOUT when a bounded
+ * mbarrier wait gave up). Asynchronous on `stream`; time it with events. */
+#define SA_PROBE_SINK_WORDS 1024
+SA_API sa_status sa_probe_stream(const void* pool, int64_t pool_entries, const int32_t* entry_ids,
+                                 int64_t n, int32_t mode, uint64_t* sink, uint32_t* status,
+                                 void* stream);
+
 #ifdef __cplusplus
 }
 #endif

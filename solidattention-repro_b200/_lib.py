@@ -121,6 +121,7 @@ PROTOTYPES = {
     "sa_ipc_export": (C.c_int, [_i32, _vp, _vp]),
     "sa_ipc_open": (C.c_int, [_i32, _vp, C.POINTER(_vp)]),
     "sa_ipc_close": (C.c_int, [_i32, _vp]),
+    "sa_probe_stream": (C.c_int, [_vp, C.c_int64, _vp, C.c_int64, _i32, _vp, _vp, _vp]),
 }
 
 _LIB = None

@@ -1104,6 +1104,15 @@ SA_API sa_status sa_ctx_step_host(sa_ctx* c, const float* query_host, const void
   return SA_OK;
 }
 
+SA_API sa_status sa_probe_stream(const void* pool, int64_t pool_entries, const int32_t* entry_ids,
+                                 int64_t n, int32_t mode, uint64_t* sink, uint32_t* status,
+                                 void* stream) {
+  static_assert(SA_PROBE_SINK_WORDS >= 1024, "sink words");
+  return launch_probe_stream(pool, pool_entries, entry_ids, n, mode,
+                             reinterpret_cast<unsigned long long*>(sink), status,
+                             static_cast<cudaStream_t>(stream));
+}
+
 SA_API sa_status sa_ctx_sync(sa_ctx* c, uint32_t* bits_out) {
   if (!c) return fail(SA_ERR_INVALID_ARG, "sync: null ctx");
   if (c->recording) return refuse_while_recording("sync");

@@ -212,6 +212,12 @@ struct SelectParams {
   int pdl;  // launched as a programmatic dependent of the previous kernel
 };
 
+// Streaming probes (sa_probe.cu): mode 0 per-lane cp.async, 1 bulk copies.
+int probe_sink_words();
+sa_status launch_probe_stream(const void* pool, long long pool_entries, const int32_t* ids,
+                              long long n, int mode, unsigned long long* sink, uint32_t* status,
+                              cudaStream_t stream);
+
 int select_max_blocks();
 // CTAs a unit's heads are split over (1 for groups of at most four heads),
 // chunks of a unit of nb_cap blocks, and the scratch bytes of the split

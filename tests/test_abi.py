@@ -100,6 +100,11 @@ def test_reference_rejections_without_a_gpu(pkg):
     # topk larger than a block
     rc = lib.sa_build_representatives(dummy, dummy, 64, 4, 2, 128, 32, 32, 33, dummy, dummy, None)
     assert rc == pkg.SA_ERR_INVALID_ARG
+    # the streaming probe: no pool, an unknown mode, an unaligned pool
+    assert lib.sa_probe_stream(None, 4, dummy, 4, 0, dummy, None, None) == pkg.SA_ERR_INVALID_ARG
+    assert lib.sa_probe_stream(dummy, 4, dummy, 4, 2, dummy, None, None) == pkg.SA_ERR_INVALID_ARG
+    assert lib.sa_probe_stream(C.c_void_p(24), 4, dummy, 4, 0, dummy, None,
+                               None) == pkg.SA_ERR_INVALID_ARG
 
 
 def test_context_config_validation_without_a_gpu(pkg):

@@ -280,3 +280,32 @@ def test_backend_variants(pkg, port):
     checksum, _ = be.execute(data, 0x5a)
     assert checksum == int((data ^ 0x5a).astype(np.uint64).sum())
     be.close()
+
+
+# ------------------------------------------------------------- streaming probe
+
+def test_streaming_probe_modes_read_the_same_bytes(pkg, cuda):
+    """sa_probe_stream: the per-lane cp.async and the bulk-copy readers fold
+    the same words of the same entries (the sink of every CTA agrees), and no
+    bounded mbarrier wait gives up."""
+    import ctypes as C
+
+    lib = pkg.load()
+    pool_entries, n = 512, 1000
+    g = torch.Generator().manual_seed(3)
+    pool = torch.randint(0, 256, (pool_entries * 16384,), dtype=torch.uint8, generator=g).to(cuda)
+    ids = torch.randint(0, pool_entries, (n,), dtype=torch.int32, generator=g).to(cuda)
+    stream = torch.cuda.current_stream(cuda)
+    sinks = []
+    for mode in (0, 1):
+        sink = torch.zeros(1024, dtype=torch.int64, device=cuda)
+        status = torch.zeros(1, dtype=torch.int32, device=cuda)
+        rc = lib.sa_probe_stream(C.c_void_p(pool.data_ptr()), pool_entries,
+                                 C.c_void_p(ids.data_ptr()), n, mode, C.c_void_p(sink.data_ptr()),
+                                 C.c_void_p(status.data_ptr()), C.c_void_p(stream.cuda_stream))
+        assert rc == 0
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        sinks.append(sink.cpu())
+    assert torch.equal(sinks[0], sinks[1])
+    assert bool(sinks[0].ne(0).any())
