@@ -292,11 +292,8 @@ __device__ __forceinline__ void load_stage(AttnSmem<G>& s, const AttnParams& p, 
 }
 
 // One plane (0: K rows, 1: V rows) of load_stage's copies. Loading a stage
-// plane by plane (all K rows, then all V rows) instead of row by row ran the
-// attention faster on plans with one whole unit per virtual CTA and about a
-// full wave (on a B200, 288 units of 129 slots: 99.5 -> 93.1 us; of 257
-// slots: 197 -> 180 us) and slower on the others (224 units on 224 virtual
-// CTAs: 43.5 -> 49.9 us; 2,304 units on 296: 376 -> 429 us).
+// plane by plane (all K rows, then all V rows) instead of row by row runs
+// the attention faster on some plans and slower on others (see launch_g).
 template <int G, bool kHeadMajor>
 __device__ __forceinline__ void load_plane(AttnSmem<G>& s, const AttnParams& p, int j, int slot,
                                            int pl, int half, int t0, int l16) {
@@ -788,11 +785,18 @@ sa_status launch_layout(const AttnParams& p, cudaStream_t stream) {
 
 template <int G>
 sa_status launch_g(const AttnParams& p, cudaStream_t stream) {
-  // stage loads plane by plane (load_plane) when every virtual CTA takes one
-  // whole unit and they fill about a wave
+  // Stages load plane by plane (load_plane) when the virtual CTAs fill about
+  // a wave, every one streams a range inside one unit (k per unit) and the
+  // ranges are long: on a B200, 288 units of 129 slots on 288 virtual CTAs
+  // 104.5 -> 94.7 us, 144 units on 288 (two per unit) 57.3 -> 54.6 us;
+  // shorter ranges (72 units on 288: 33.7 -> 34.0 us; 36 on 288: 19.6 ->
+  // 21.7 us), several units per CTA (2,304 units on 296: 368 -> 439 us) or
+  // a part of the SMs idle (224 units on 224: 43.4 -> 49.9 us) run slower.
   const long long units = (long long)p.num_sl * p.kv_heads;
+  const long long slots = units * p.slots_per_unit;
   const long long wave = (long long)device_sm_count() * virt_ctas<G>();
-  const bool plane_order = units == p.ctas && (long long)p.ctas * 10 >= wave * 9;
+  const bool plane_order = (long long)p.ctas * 10 >= wave * 9 && p.ctas % units == 0 &&
+                           slots >= 64LL * p.ctas;
   if (p.head_major)
     return plane_order ? launch_layout<G, true, true>(p, stream)
                        : launch_layout<G, true, false>(p, stream);
