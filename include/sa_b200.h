@@ -315,7 +315,12 @@ SA_API sa_status sa_ctx_step_raw(sa_ctx* ctx, const float* q_raw, const float* k
                                  const int32_t* positions, float rope_theta, float norm_eps,
                                  void* out);
 /* The same step from host buffers: H2D inputs, step, D2H output, synchronize
- * (the end-to-end call of a host-side decode loop). */
+ * (the end-to-end call of a host-side decode loop). Pinned (mapped) buffers
+ * are used in place except the queries, which are copied; with all three
+ * pinned, no peer gather attached and a non-legacy stream, the first call
+ * records the copy and the step's launches into a CUDA graph and later calls
+ * with the same buffers replay it. Pageable buffers go through staging
+ * copies on every call. */
 SA_API sa_status sa_ctx_step_host(sa_ctx* ctx, const float* query_host,
                                   const void* kv_new_host, int32_t kv_fp32,
                                   void* out_host);
